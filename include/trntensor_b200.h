@@ -1,0 +1,99 @@
+/*
+ * trntensor_b200 C ABI.
+ *
+ * Drop-in device boundary for the trntensor DF-MP2 / AO->MO hot path on
+ * NVIDIA B200 (sm_100a). Every entry point:
+ *   - takes plain device pointers, sizes and a CUDA stream (cudaStream_t
+ *     passed as void*; NULL = legacy default stream);
+ *   - enqueues work asynchronously on that stream and returns a status code
+ *     (TT_OK == 0) describing argument checks and launch errors only;
+ *   - allocates no memory: outputs and workspaces are owned by the caller,
+ *     whose sizes the *_workspace_bytes queries give;
+ *   - never falls back to another implementation.
+ * Device-side waits are bounded; a wait that runs out writes a nonzero code
+ * into the caller's int `dev_status` (device memory), which the caller reads
+ * after synchronising.
+ *
+ * Layouts are those of the reference's torch tensors (row-major, contiguous):
+ *   B       (nocc, nvir, naux)      eri (nbf, nbf, naux)
+ *   C_occ   (nbf, nocc)             C_vir (nbf, nvir)
+ */
+#ifndef TRNTENSOR_B200_H_
+#define TRNTENSOR_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TT_OK 0
+#define TT_ERR_NULL 1        /* a required pointer is NULL */
+#define TT_ERR_SHAPE 2       /* a size is out of range */
+#define TT_ERR_ALIGN 3       /* a pointer is not 16-byte aligned */
+#define TT_ERR_WORKSPACE 4   /* workspace too small */
+#define TT_ERR_DEVICE 5      /* current device is not sm_100 */
+#define TT_ERR_CUDA 6        /* CUDA runtime / launch error */
+#define TT_ERR_TMA 7         /* tensor-map encoding failed */
+
+/* Human-readable text for a status code. */
+const char* tt_status_string(int status);
+/* Library ABI version (major * 10000 + minor * 100 + patch). */
+int tt_version(void);
+/* TT_OK when the current CUDA device can run this library (sm_100). */
+int tt_device_check(void);
+/* Text of the last CUDA error seen by this thread's calls ("" if none). */
+const char* tt_last_cuda_error(void);
+
+/* Number of unordered occupied pairs i <= j: nocc * (nocc + 1) / 2. */
+long long tt_mp2_num_pairs(int nocc);
+
+/* Workspace bytes tt_mp2_energy_f32 needs: hi and lo tf32 copies of B with
+ * naux padded to a multiple of 16. */
+size_t tt_mp2_workspace_bytes(int nocc, int nvir, int naux);
+
+/* Split x (rows x cols, row-major) into hi = tf32(x), lo = tf32(x - hi),
+ * written as rows x cols_pad with zero padding (cols_pad >= cols, % 4 == 0). */
+int tt_split_tf32(const float* x, float* hi, float* lo, long long rows, int cols, int cols_pad,
+                  void* stream);
+
+/*
+ * DF-MP2 correlation energy, fp32 inputs, 3xTF32 tcgen05 tensor cores.
+ *   *energy = sum over the unordered pairs [pair_begin, pair_end) (linear
+ *             id of (i, j), i <= j, row-major; the full sum is
+ *             [0, tt_mp2_num_pairs(nocc))) of w_ij * E_ij, w = 2 for i < j,
+ *             1 for i == j, E_ij = sum_ab T_ab (2T_ab - T_ba) / D_ijab.
+ *   pair_partials (nullable, nocc*nocc doubles): E_ij written at [i][j] and
+ *             [j][i] for the visited pairs, zero elsewhere.
+ * energy, pair_partials and dev_status are zeroed by the call.
+ * Replaces trntensor/nki/dispatch.py:240-283 (_nki_mp2_energy) and the
+ * device kernel trntensor/nki/_kernels.py:119-207 (mp2_energy_kernel).
+ */
+int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir, int nocc,
+                      int nvir, int naux, long long pair_begin, long long pair_end,
+                      void* workspace, size_t workspace_bytes, double* energy,
+                      double* pair_partials, int* dev_status, void* stream);
+
+/* As tt_mp2_energy_f32, with B already split by tt_split_tf32 into
+ * (nocc, nvir, naux_pad) hi/lo arrays (naux_pad % 16 == 0). */
+int tt_mp2_energy_presplit_f32(const float* B_hi, const float* B_lo, int naux_pad,
+                               const float* eps_occ, const float* eps_vir, int nocc, int nvir,
+                               long long pair_begin, long long pair_end, double* energy,
+                               double* pair_partials, int* dev_status, void* stream);
+
+/* DF-MP2 energy in fp64 throughout (precision="kahan" semantics of
+ * trntensor/einsum.py:108-111 applied to trntensor/quantum.py:87-100). */
+int tt_mp2_energy_f64(const double* B, const double* eps_occ, const double* eps_vir, int nocc,
+                      int nvir, int naux, long long pair_begin, long long pair_end,
+                      double* energy, double* pair_partials, void* stream);
+
+/* Same sum on CUDA cores in plain fp32 FMA; an independent on-device check
+ * of tt_mp2_energy_f32, not a production path. */
+int tt_mp2_energy_simt_f32(const float* B, const float* eps_occ, const float* eps_vir, int nocc,
+                           int nvir, int naux, long long pair_begin, long long pair_end,
+                           double* energy, double* pair_partials, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TRNTENSOR_B200_H_ */

@@ -1,0 +1,204 @@
+"""Host-side behaviour that needs no GPU: validation messages kept from the
+reference (tests/test_quantum.py:35-47,95-110), precision handling, planner
+and einsum semantics, and the C-ABI symbol table."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import trntensor_b200 as tt
+from trntensor_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+class TestMp2Validation:
+    def test_shape_errors(self):
+        B3 = torch.randn(3, 4, 5)
+        eo, ev = torch.randn(3), torch.randn(4)
+        with pytest.raises(ValueError, match="must be 3D"):
+            tt.mp2_energy(torch.randn(3, 4), eo, ev)
+        with pytest.raises(ValueError, match="eps_occ"):
+            tt.mp2_energy(B3, torch.randn(2), ev)
+        with pytest.raises(ValueError, match="eps_vir"):
+            tt.mp2_energy(B3, eo, torch.randn(5))
+
+    def test_precision_errors(self):
+        B3 = torch.randn(3, 4, 5)
+        with pytest.raises(ValueError, match="precision must be"):
+            tt.mp2_energy(B3, torch.randn(3), torch.randn(4), precision="bogus")
+        with pytest.raises(NotImplementedError, match="kahan"):
+            tt.mp2_energy(B3, torch.randn(3), torch.randn(4), precision="dd")
+
+    def test_empty_is_zero(self):
+        e = tt.mp2_energy(torch.randn(0, 4, 5), torch.randn(0), torch.randn(4))
+        assert e.shape == () and float(e) == 0.0
+
+
+class TestAoToMoValidation:
+    def test_shape_errors(self):
+        eri, co, cv = torch.randn(6, 6, 8), torch.randn(6, 2), torch.randn(6, 3)
+        with pytest.raises(ValueError, match="must be 3D"):
+            tt.ao_to_mo_transform(torch.randn(6, 6), co, cv)
+        with pytest.raises(ValueError, match="first two dims must match"):
+            tt.ao_to_mo_transform(torch.randn(6, 7, 8), co, cv)
+        with pytest.raises(ValueError, match="C_occ"):
+            tt.ao_to_mo_transform(eri, torch.randn(5, 2), cv)
+        with pytest.raises(ValueError, match="C_vir"):
+            tt.ao_to_mo_transform(eri, co, torch.randn(7, 3))
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error path")
+def test_no_cpu_fallback():
+    """Without a CUDA device the primitives raise instead of computing on CPU."""
+    with pytest.raises(RuntimeError, match="CUDA"):
+        tt.mp2_energy(torch.randn(2, 3, 4), torch.randn(2), torch.randn(3))
+
+
+class TestPlanner:
+    def test_matmul_and_bmm(self):
+        p = tt.plan_contraction("ap,bp->ab", torch.randn(4, 6), torch.randn(5, 6))
+        assert p.strategy == "matmul" and p.transB and not p.transA
+        assert p.backend == "pytorch"
+        p = tt.plan_contraction("bij,bjk->bik", torch.randn(2, 3, 4), torch.randn(2, 4, 5))
+        assert p.strategy == "bmm"
+        p = tt.plan_contraction("mi,mnP->inP", torch.randn(4, 2), torch.randn(4, 4, 3))
+        assert p.strategy == "torch"
+
+    def test_cache(self):
+        tt.clear_plan_cache()
+        a, b = torch.randn(3, 4), torch.randn(4, 5)
+        p1 = tt.plan_contraction("ij,jk->ik", a, b)
+        p2 = tt.plan_contraction("ij,jk->ik", a, b)
+        assert p1 is p2 and tt.plan_cache_info() == {"size": 1}
+        tt.plan_contraction("ij,jk->ik", a, b, precision="kahan")
+        assert tt.plan_cache_info()["size"] == 2
+        tt.clear_plan_cache()
+        assert tt.plan_cache_info()["size"] == 0
+
+    def test_greedy_order(self):
+        from trntensor_b200.plan import _greedy_path_search
+
+        sizes = {"i": 100, "j": 200, "k": 5, "l": 50}
+        assert _greedy_path_search(["ij", "jk", "kl"], "il", sizes)[0] == (1, 2)
+        sizes["m"] = 3
+        assert _greedy_path_search(["ij", "jk", "kl", "lm"], "im", sizes)[0] == (2, 3)
+
+    def test_validation_messages(self):
+        a, b = torch.randn(3, 4), torch.randn(4, 5)
+        with pytest.raises(ValueError, match="2 operand term"):
+            tt.plan_contraction("ij,jk->ik", a)
+        with pytest.raises(ValueError, match="operand 1"):
+            tt.plan_contraction("ij,jk->ik", a, torch.randn(4))
+        with pytest.raises(ValueError, match="index 'j'"):
+            tt.plan_contraction("ij,jk->ik", a, torch.randn(5, 5))
+        with pytest.raises(ValueError, match="invalid characters"):
+            tt.plan_contraction("i1,jk->ik", a, b)
+        with pytest.raises(ValueError, match="precision must be"):
+            tt.plan_contraction("ij,jk->ik", a, b, precision="x")
+
+    def test_estimate_flops(self):
+        assert tt.estimate_flops("ij,jk->ik", torch.randn(10, 20), torch.randn(20, 30)) == 6000
+
+
+class TestEinsum:
+    def test_strategies_match_torch(self):
+        torch.manual_seed(0)
+        a, b = torch.randn(5, 7), torch.randn(6, 7)
+        torch.testing.assert_close(tt.einsum("ap,bp->ab", a, b), a @ b.T)
+        x, y = torch.randn(3, 4, 5), torch.randn(3, 5, 2)
+        torch.testing.assert_close(tt.einsum("bij,bjk->bik", x, y), torch.bmm(x, y))
+        c, d, e = torch.randn(4, 5), torch.randn(5, 6), torch.randn(6, 3)
+        torch.testing.assert_close(tt.einsum("ij,jk,kl->il", c, d, e), c @ d @ e)
+
+    def test_alpha_beta_out_dtype(self):
+        a, b, c = torch.randn(3, 4), torch.randn(4, 5), torch.randn(3, 5)
+        torch.testing.assert_close(
+            tt.einsum("ij,jk->ik", a, b, alpha=2.0, beta=0.5, out=c), 2 * (a @ b) + 0.5 * c
+        )
+        assert tt.einsum("ij,jk->ik", a, b, dtype="bf16").dtype == torch.bfloat16
+        with pytest.raises(ValueError, match="unknown dtype"):
+            tt.einsum("ij,jk->ik", a, b, dtype="int3")
+
+    def test_precision(self):
+        a, b = torch.randn(3, 4), torch.randn(4, 5)
+        r = tt.einsum("ij,jk->ik", a, b, precision="kahan")
+        assert r.dtype == torch.float32
+        torch.testing.assert_close(r, (a.double() @ b.double()).float())
+        with pytest.raises(NotImplementedError, match="kahan"):
+            tt.einsum("ij,jk->ik", a, b, precision="dd")
+
+    def test_multi_einsum(self):
+        B = torch.randn(3, 4, 5)
+        r = tt.multi_einsum(("iap,jbp->ijab", B, B), ("ibp,jap->ijab", B, B))
+        torch.testing.assert_close(r[0], torch.einsum("iap,jbp->ijab", B, B))
+        torch.testing.assert_close(r[1], torch.einsum("ibp,jap->ijab", B, B))
+
+
+class TestBackendSurface:
+    def test_namespace_matches_reference(self):
+        ref_all = {
+            "einsum", "multi_einsum", "ContractionPlan", "plan_contraction", "estimate_flops",
+            "clear_plan_cache", "plan_cache_info", "cp_decompose", "cp_reconstruct",
+            "tucker_decompose", "tucker_reconstruct", "tt_decompose", "tt_reconstruct",
+            "HAS_NKI", "set_backend", "get_backend", "to_xla", "from_xla", "mp2_energy",
+            "ao_to_mo_transform",
+        }
+        assert ref_all <= set(tt.__all__)
+        from trntensor_b200.nki.dispatch import HAS_NKI
+
+        assert HAS_NKI is False
+
+    def test_set_backend(self):
+        tt.set_backend("pytorch")
+        assert tt.get_backend() == "pytorch"
+        tt.set_backend("auto")
+        with pytest.raises(RuntimeError, match="NKI"):
+            tt.set_backend("nki")
+        with pytest.raises(ValueError):
+            tt.set_backend("tpu")
+        with pytest.raises(RuntimeError):
+            tt.to_xla(torch.randn(2))
+        x = torch.randn(2)
+        assert tt.from_xla(x) is x
+
+    def test_decompositions_out_of_scope(self):
+        with pytest.raises(NotImplementedError):
+            tt.cp_decompose(torch.randn(3, 3, 3), rank=2)
+
+
+class TestCAbi:
+    def _declared(self):
+        hdrs = sorted((ROOT / "include").glob("*.h"))
+        names = set()
+        for h in hdrs:
+            txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+            names |= set(re.findall(r"\b(tt_\w+)\s*\(", txt))
+        return names
+
+    def test_library_exports_every_declared_symbol(self):
+        lib = _lib.load()
+        declared = self._declared()
+        assert declared, "no declarations found"
+        missing = [n for n in declared if not hasattr(lib, n)]
+        assert not missing, missing
+        assert declared == set(_lib.SIGNATURES), declared ^ set(_lib.SIGNATURES)
+
+    def test_host_only_calls(self):
+        lib = _lib.load()
+        assert lib.tt_version() >= 100
+        assert lib.tt_mp2_num_pairs(256) == 32896
+        assert lib.tt_mp2_workspace_bytes(2, 3, 5) == 2 * 2 * 3 * 16 * 4
+        assert lib.tt_status_string(0) == b"ok"
+        # argument checks happen before any CUDA call
+        assert lib.tt_mp2_energy_f64(None, None, None, 1, 1, 1, 0, 1, None, None, None) == 1
+        null = ctypes.c_void_p(16)
+        assert lib.tt_mp2_energy_f32(null, null, null, 4, 4, 4, 0, 11, null, 10**9, null, None,
+                                     null, None) == 2
+        assert lib.tt_mp2_energy_f32(null, null, null, 4, 4, 4, 0, 10, null, 8, null, None,
+                                     null, None) == 4

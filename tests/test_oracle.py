@@ -1,0 +1,79 @@
+"""The CPU oracle against golden vectors produced by the reference itself."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests.helpers import AO_CASES, MP2_CASES, ao_case_inputs, mp2_case_inputs, ref_recipe_mp2
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_mp2_loop_fp32_matches_reference(golden, name):
+    B, eo, ev = (t.numpy() for t in mp2_case_inputs(golden, name))
+    e, _ = oracle.mp2_energy_loop(B, eo, ev)
+    ref = golden[f"{name}/e_fp32"]
+    assert abs(float(e) - ref) <= 2e-6 * abs(ref)
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_mp2_fp64_and_pairs_match_reference(golden, name):
+    B, eo, ev = (t.numpy() for t in mp2_case_inputs(golden, name))
+    e, part = oracle.mp2_energy_fp64(B, eo, ev)
+    np.testing.assert_allclose(e, golden[f"{name}/e_fp64"], rtol=1e-12)
+    np.testing.assert_allclose(part, golden[f"{name}/pair_fp64"], rtol=1e-10, atol=1e-14)
+    e2, part2 = oracle.mp2_energy_loop(B, eo, ev, dtype=np.float64)
+    np.testing.assert_allclose(e2, e, rtol=1e-12)
+    np.testing.assert_allclose(part2, part, rtol=1e-10, atol=1e-14)
+
+
+def test_manual_unrolled_kat(golden):
+    """tests/test_quantum.py:11-33: the loop equals the explicit 4-index sum."""
+    B, eo, ev = (t.numpy() for t in mp2_case_inputs(golden, "kat_manual"))
+    e, _ = oracle.mp2_energy_loop(B, eo, ev)
+    np.testing.assert_allclose(float(e), golden["kat_manual/e_unrolled"], rtol=1e-6, atol=1e-6)
+
+
+def test_tutorial_value():
+    """docs/tutorial_df_mp2.md:77: E_MP2 = -50.5432928801 for (5,19,72), seed 42."""
+    B, eo, ev = (t.numpy() for t in ref_recipe_mp2(42, 5, 19, 72))
+    e, _ = oracle.mp2_energy_loop(B, eo, ev)
+    assert abs(float(e) - (-50.5432928801)) < 1e-5
+    e64, _ = oracle.mp2_energy_fp64(B, eo, ev)
+    assert abs(e64 - (-50.5432928801)) / 50.54 < 1e-6
+
+
+def test_regenerated_inputs_match(golden):
+    for name in MP2_CASES:
+        B, eo, ev = mp2_case_inputs(golden, name)
+        assert tuple(B.shape) == tuple(golden[f"{name}/shape"])
+
+
+@pytest.mark.parametrize("name", sorted(AO_CASES))
+def test_ao2mo_two_step_matches_reference(golden, name):
+    vals = ao_case_inputs(golden, name)
+    eri, co, cv = (v.double().numpy() for v in vals[:3])
+    B, _ = oracle.ao_to_mo_two_step(eri, co, cv)
+    if f"{name}/B_fp64" in golden:
+        ref = golden[f"{name}/B_fp64"]
+        np.testing.assert_allclose(B, ref, rtol=1e-10, atol=1e-12 * np.abs(ref).max())
+        if B.size < 5000:
+            np.testing.assert_allclose(oracle.ao_to_mo_fused(eri, co, cv), ref, rtol=1e-9,
+                                       atol=1e-12 * np.abs(ref).max())
+    else:
+        idx = golden[f"{name}/B_fp64_sample_idx"]
+        np.testing.assert_allclose(B.flatten()[idx], golden[f"{name}/B_fp64_sample"], rtol=1e-10,
+                                   atol=1e-14)
+    if f"{name}/e_fp64" in golden:
+        eo, ev = (v.double().numpy() for v in vals[3:])
+        e, _ = oracle.mp2_energy_fp64(B, eo, ev)
+        np.testing.assert_allclose(e, golden[f"{name}/e_fp64"], rtol=1e-10)
+
+
+def test_config1_inputs_are_orthonormal_and_symmetric():
+    eri, co, cv = AO_CASES["config1"]()
+    C = torch.cat([co, cv], 1).double()
+    torch.testing.assert_close(C.T @ C, torch.eye(128, dtype=torch.float64), atol=1e-6, rtol=0)
+    torch.testing.assert_close(eri, eri.transpose(0, 1))

@@ -1,0 +1,227 @@
+// C-ABI entry points for the DF-MP2 energy (tensor-core 3xTF32, fp64 and
+// fp32 CUDA-core variants) and the tf32 hi/lo split.
+#include "common.cuh"
+#include "mp2_simt.cuh"
+#include "mp2_tf32.cuh"
+
+namespace tt {
+
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// hi = tf32(x), lo = tf32(x - hi); rows x cols -> rows x cols_pad, zero pad.
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo, long long rows, int cols,
+                                  int cols_pad) {
+  const long long nvec = rows * (long long)(cols_pad / 4);
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < nvec;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long r = v / (cols_pad / 4);
+    const int c = (int)(v % (cols_pad / 4)) * 4;
+    float in[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) in[k] = (c + k < cols) ? __ldg(x + r * cols + c + k) : 0.f;
+    float4 h, l;
+    h.x = to_tf32(in[0]); l.x = to_tf32(in[0] - h.x);
+    h.y = to_tf32(in[1]); l.y = to_tf32(in[1] - h.y);
+    h.z = to_tf32(in[2]); l.z = to_tf32(in[2] - h.z);
+    h.w = to_tf32(in[3]); l.w = to_tf32(in[3] - h.w);
+    reinterpret_cast<float4*>(hi + r * cols_pad)[c / 4] = h;
+    reinterpret_cast<float4*>(lo + r * cols_pad)[c / 4] = l;
+  }
+}
+
+namespace {
+std::once_flag g_mp2_attr_flags[kMaxDevices];
+int g_mp2_attr_ok[kMaxDevices];
+int g_num_sms[kMaxDevices];
+
+int mp2_setup(int dev) {
+  return once_per_device(g_mp2_attr_flags, g_mp2_attr_ok, dev, [dev]() -> int {
+    if (cudaFuncSetAttribute(mp2::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mp2::kSmemBytes) != cudaSuccess)
+      return TT_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev) !=
+        cudaSuccess)
+      return TT_ERR_CUDA;
+    return TT_OK;
+  });
+}
+
+inline int naux_padded(int naux) { return (naux + 15) / 16 * 16; }
+
+int check_pairs(int nocc, long long pb, long long pe) {
+  const long long np = (long long)nocc * (nocc + 1) / 2;
+  if (pb < 0 || pe < pb || pe > np) return TT_ERR_SHAPE;
+  return TT_OK;
+}
+}  // namespace
+
+int launch_split(const float* x, float* hi, float* lo, long long rows, int cols, int cols_pad,
+                 cudaStream_t s, int num_sms) {
+  const long long nvec = rows * (long long)(cols_pad / 4);
+  if (nvec == 0) return TT_OK;
+  long long blocks = (nvec + 255) / 256;
+  const long long cap = (long long)num_sms * 16;
+  if (blocks > cap) blocks = cap;
+  split_tf32_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, hi, lo, rows, cols, cols_pad);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace tt
+
+using namespace tt;
+
+extern "C" {
+
+long long tt_mp2_num_pairs(int nocc) {
+  return nocc > 0 ? (long long)nocc * (nocc + 1) / 2 : 0;
+}
+
+size_t tt_mp2_workspace_bytes(int nocc, int nvir, int naux) {
+  if (nocc <= 0 || nvir <= 0 || naux <= 0) return 0;
+  return 2ull * (size_t)nocc * (size_t)nvir * (size_t)naux_padded(naux) * sizeof(float);
+}
+
+int tt_split_tf32(const float* x, float* hi, float* lo, long long rows, int cols, int cols_pad,
+                  void* stream) {
+  if (!x || !hi || !lo) return TT_ERR_NULL;
+  if (rows < 0 || cols <= 0 || cols_pad < cols || cols_pad % 4 != 0) return TT_ERR_SHAPE;
+  if (!aligned16(hi) || !aligned16(lo)) return TT_ERR_ALIGN;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = mp2_setup(dev);
+  if (st != TT_OK) return st;
+  return launch_split(x, hi, lo, rows, cols, cols_pad, (cudaStream_t)stream, g_num_sms[dev]);
+}
+
+int tt_mp2_energy_presplit_f32(const float* B_hi, const float* B_lo, int naux_pad,
+                               const float* eps_occ, const float* eps_vir, int nocc, int nvir,
+                               long long pair_begin, long long pair_end, double* energy,
+                               double* pair_partials, int* dev_status, void* stream) {
+  if (!B_hi || !B_lo || !eps_occ || !eps_vir || !energy || !dev_status) return TT_ERR_NULL;
+  if (nocc <= 0 || nvir <= 0 || naux_pad <= 0 || naux_pad % 16 != 0) return TT_ERR_SHAPE;
+  if (nocc > 65535 || nvir > 65535) return TT_ERR_SHAPE;
+  if (check_pairs(nocc, pair_begin, pair_end) != TT_OK) return TT_ERR_SHAPE;
+  if (!aligned16(B_hi) || !aligned16(B_lo)) return TT_ERR_ALIGN;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = mp2_setup(dev);
+  if (st != TT_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  TT_CUDA(cudaMemsetAsync(energy, 0, sizeof(double), s));
+  TT_CUDA(cudaMemsetAsync(dev_status, 0, sizeof(int), s));
+  if (pair_partials)
+    TT_CUDA(cudaMemsetAsync(pair_partials, 0, sizeof(double) * (size_t)nocc * nocc, s));
+  if (pair_end == pair_begin) return TT_OK;
+
+  // Tensor maps over (naux_pad, nvir, nocc), innermost first; 64-byte rows
+  // with 64B swizzle, boxes of 128 (A operand) and 256 (B operand) rows.
+  CUtensorMap mA_hi, mA_lo, mB_hi, mB_lo;
+  const uint64_t dims[3] = {(uint64_t)naux_pad, (uint64_t)nvir, (uint64_t)nocc};
+  const uint64_t strides[2] = {(uint64_t)naux_pad * 4, (uint64_t)naux_pad * 4 * nvir};
+  const uint32_t boxA[3] = {(uint32_t)mp2::kKC, (uint32_t)mp2::kM, 1};
+  const uint32_t boxB[3] = {(uint32_t)mp2::kKC, (uint32_t)mp2::kN, 1};
+  if (encode_tmap(&mA_hi, B_hi, 3, dims, strides, boxA, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      encode_tmap(&mA_lo, B_lo, 3, dims, strides, boxA, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      encode_tmap(&mB_hi, B_hi, 3, dims, strides, boxB, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      encode_tmap(&mB_lo, B_lo, 3, dims, strides, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
+    return TT_ERR_TMA;
+
+  mp2::Params p;
+  p.eps_occ = eps_occ;
+  p.eps_vir = eps_vir;
+  p.nocc = nocc;
+  p.nvir = nvir;
+  p.naux_pad = naux_pad;
+  p.pair_begin = pair_begin;
+  p.pair_end = pair_end;
+  p.n_rects = mp2::rect_count(nvir);
+  p.energy = energy;
+  p.pair_partials = pair_partials;
+  p.err = dev_status;
+  const long long n_items = (pair_end - pair_begin) * (long long)p.n_rects;
+  const int grid = (int)(n_items < g_num_sms[dev] ? n_items : g_num_sms[dev]);
+  mp2::energy_kernel<<<grid, mp2::kThreads, mp2::kSmemBytes, s>>>(mA_hi, mA_lo, mB_hi, mB_lo, p);
+  return cuda_status(cudaGetLastError());
+}
+
+int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir, int nocc,
+                      int nvir, int naux, long long pair_begin, long long pair_end,
+                      void* workspace, size_t workspace_bytes, double* energy,
+                      double* pair_partials, int* dev_status, void* stream) {
+  if (!B || !workspace || !eps_occ || !eps_vir || !energy || !dev_status) return TT_ERR_NULL;
+  if (nocc <= 0 || nvir <= 0 || naux <= 0) return TT_ERR_SHAPE;
+  if (nocc > 65535 || nvir > 65535) return TT_ERR_SHAPE;
+  if (check_pairs(nocc, pair_begin, pair_end) != TT_OK) return TT_ERR_SHAPE;
+  const size_t need = tt_mp2_workspace_bytes(nocc, nvir, naux);
+  if (workspace_bytes < need) return TT_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return TT_ERR_ALIGN;
+  const int naux_pad = naux_padded(naux);
+  float* hi = static_cast<float*>(workspace);
+  float* lo = hi + (size_t)nocc * nvir * naux_pad;
+  int st = tt_split_tf32(B, hi, lo, (long long)nocc * nvir, naux, naux_pad, stream);
+  if (st != TT_OK) return st;
+  return tt_mp2_energy_presplit_f32(hi, lo, naux_pad, eps_occ, eps_vir, nocc, nvir, pair_begin,
+                                    pair_end, energy, pair_partials, dev_status, stream);
+}
+
+}  // extern "C"
+
+namespace {
+template <typename T>
+int launch_simt(const T* B, const T* eps_occ, const T* eps_vir, int nocc, int nvir, int naux,
+                long long pair_begin, long long pair_end, double* energy, double* pair_partials,
+                void* stream) {
+  if (!B || !eps_occ || !eps_vir || !energy) return TT_ERR_NULL;
+  if (nocc <= 0 || nvir <= 0 || naux <= 0) return TT_ERR_SHAPE;
+  if (check_pairs(nocc, pair_begin, pair_end) != TT_OK) return TT_ERR_SHAPE;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = mp2_setup(dev);
+  if (st != TT_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  TT_CUDA(cudaMemsetAsync(energy, 0, sizeof(double), s));
+  if (pair_partials)
+    TT_CUDA(cudaMemsetAsync(pair_partials, 0, sizeof(double) * (size_t)nocc * nocc, s));
+  if (pair_end == pair_begin) return TT_OK;
+  mp2s::Params<T> p;
+  p.B = B;
+  p.eps_occ = eps_occ;
+  p.eps_vir = eps_vir;
+  p.nocc = nocc;
+  p.nvir = nvir;
+  p.naux = naux;
+  p.pair_begin = pair_begin;
+  p.pair_end = pair_end;
+  p.nblk = (nvir + mp2s::kT - 1) / mp2s::kT;
+  p.energy = energy;
+  p.pair_partials = pair_partials;
+  const long long n_items = (pair_end - pair_begin) * (long long)(p.nblk * (p.nblk + 1) / 2);
+  const long long cap = (long long)g_num_sms[dev] * 8;
+  const int grid = (int)(n_items < cap ? n_items : cap);
+  mp2s::energy_kernel<T><<<grid, mp2s::kThreads, 0, s>>>(p);
+  return cuda_status(cudaGetLastError());
+}
+}  // namespace
+
+extern "C" {
+int tt_mp2_energy_f64(const double* B, const double* eps_occ, const double* eps_vir, int nocc,
+                      int nvir, int naux, long long pair_begin, long long pair_end,
+                      double* energy, double* pair_partials, void* stream) {
+  return launch_simt<double>(B, eps_occ, eps_vir, nocc, nvir, naux, pair_begin, pair_end, energy,
+                             pair_partials, stream);
+}
+int tt_mp2_energy_simt_f32(const float* B, const float* eps_occ, const float* eps_vir, int nocc,
+                           int nvir, int naux, long long pair_begin, long long pair_end,
+                           double* energy, double* pair_partials, void* stream) {
+  return launch_simt<float>(B, eps_occ, eps_vir, nocc, nvir, naux, pair_begin, pair_end, energy,
+                            pair_partials, stream);
+}
+}  // extern "C"

@@ -1,0 +1,166 @@
+"""Device dispatch: torch tensors in, C-ABI calls out.
+
+This module takes the place of the reference's backend selector and its
+device wrappers (trntensor/nki/dispatch.py:240-336, ``_nki_mp2_energy`` and
+``_nki_ao_to_mo_transform``). Differences by design:
+
+* the only executor is the sm_100a library (``libtrntensor_b200.so``);
+  there is no CPU fallback and no FLOP threshold;
+* host tensors are copied to the current CUDA device and results come back
+  to the caller's device, like the reference's ``_to_xla``/``.to(orig)``;
+* every buffer the kernels touch is allocated here through torch's caching
+  allocator; the library itself never allocates.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+
+HAS_NKI = False  # the Trainium NKI runtime is never used by this package
+
+_backend = "auto"
+_VALID_BACKENDS = ("auto", "cuda", "pytorch", "nki")
+
+
+def set_backend(backend: str) -> None:
+    """Select the executor for the generic ``einsum`` strategies.
+
+    Mirrors trntensor/nki/dispatch.py:94-101. ``"auto"``/``"cuda"`` route the
+    matmul-shaped plans to CUDA tensors' native kernels, ``"pytorch"`` keeps
+    them on whatever device the operands live on. ``"nki"`` raises, exactly as
+    the reference does on a host without neuronxcc. The two DF-MP2 primitives
+    always run on the sm_100a library.
+    """
+    global _backend
+    if backend not in _VALID_BACKENDS:
+        raise ValueError(f"backend must be one of {_VALID_BACKENDS}; got {backend!r}")
+    if backend == "nki":
+        raise RuntimeError(
+            "NKI backend requires neuronxcc (AWS Trainium); this build runs on NVIDIA B200"
+        )
+    _backend = backend
+
+
+def get_backend() -> str:
+    return _backend
+
+
+def to_xla(tensor: torch.Tensor) -> torch.Tensor:
+    """Trainium residency helper (trntensor/nki/dispatch.py:152-176).
+
+    There is no XLA device here; raises like the reference does without NKI.
+    On B200, residency is simply a CUDA tensor: use ``tensor.cuda()``.
+    """
+    if tensor.device.type == "xla":
+        return tensor
+    raise RuntimeError(
+        "to_xla requires the NKI runtime. On B200 keep operands resident with tensor.cuda()."
+    )
+
+
+def from_xla(tensor: torch.Tensor) -> torch.Tensor:
+    """Move a tensor back to CPU; no-op if already on CPU (dispatch.py:179-184)."""
+    if tensor.device.type == "cpu":
+        return tensor
+    return tensor.to("cpu")
+
+
+def _device() -> torch.device:
+    if not torch.cuda.is_available():
+        raise RuntimeError(
+            "trntensor_b200 needs a CUDA device (NVIDIA B200, sm_100a); no CUDA device is visible "
+            "and there is no CPU fallback"
+        )
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _stream_handle() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _to_dev(t: torch.Tensor, dev: torch.device, dtype: torch.dtype) -> torch.Tensor:
+    if t.device != dev:
+        t = t.to(dev, non_blocking=t.is_pinned())
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    return t.contiguous()
+
+
+def _check_status(dev_status: torch.Tensor, what: str) -> None:
+    if os.environ.get("TRNTENSOR_B200_ASYNC", "") in ("1", "true", "yes"):
+        return
+    code = int(dev_status.item())
+    if code != 0:
+        raise _lib.DeviceError(f"{what}: device wait ran out (status 0x{code:x})")
+
+
+def mp2_compute_dtype(B: torch.Tensor, precision: str) -> torch.dtype:
+    if precision == "kahan" or B.dtype == torch.float64:
+        return torch.float64
+    return torch.float32
+
+
+def _cuda_mp2_energy(
+    B: torch.Tensor,
+    eps_occ: torch.Tensor,
+    eps_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+    pair_range: tuple[int, int] | None = None,
+    return_partials: bool = False,
+    kernel: str = "tc",
+):
+    """Run the DF-MP2 energy on the current CUDA device.
+
+    Returns ``(energy_fp64_device_scalar, partials_or_None)``; both stay on the
+    device. ``pair_range`` selects a half-open range of unordered pair ids
+    (i <= j, row-major) for sharding. ``kernel="simt"`` selects the CUDA-core
+    fp32 cross-check kernel instead of the tensor-core one.
+    """
+    lib = _lib.load()
+    dev = _device()
+    cdt = mp2_compute_dtype(B, precision)
+    nocc, nvir, naux = (int(s) for s in B.shape)
+    Bd = _to_dev(B, dev, cdt)
+    eo = _to_dev(eps_occ, dev, cdt)
+    ev = _to_dev(eps_vir, dev, cdt)
+    npairs = int(lib.tt_mp2_num_pairs(nocc))
+    pb, pe = (0, npairs) if pair_range is None else (int(pair_range[0]), int(pair_range[1]))
+    energy = torch.empty((), dtype=torch.float64, device=dev)
+    partials = (
+        torch.empty((nocc, nocc), dtype=torch.float64, device=dev) if return_partials else None
+    )
+    stream = ctypes.c_void_p(_stream_handle())
+    if cdt == torch.float64:
+        st = lib.tt_mp2_energy_f64(
+            _ptr(Bd), _ptr(eo), _ptr(ev), nocc, nvir, naux, pb, pe,
+            _ptr(energy), _ptr(partials), stream,
+        )
+        _lib.check(st, "tt_mp2_energy_f64")
+        return energy, partials
+    if kernel == "simt":
+        st = lib.tt_mp2_energy_simt_f32(
+            _ptr(Bd), _ptr(eo), _ptr(ev), nocc, nvir, naux, pb, pe,
+            _ptr(energy), _ptr(partials), stream,
+        )
+        _lib.check(st, "tt_mp2_energy_simt_f32")
+        return energy, partials
+    ws_bytes = int(lib.tt_mp2_workspace_bytes(nocc, nvir, naux))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    dev_status = torch.empty((), dtype=torch.int32, device=dev)
+    st = lib.tt_mp2_energy_f32(
+        _ptr(Bd), _ptr(eo), _ptr(ev), nocc, nvir, naux, pb, pe,
+        _ptr(ws), ws_bytes, _ptr(energy), _ptr(partials), _ptr(dev_status), stream,
+    )
+    _lib.check(st, "tt_mp2_energy_f32")
+    _check_status(dev_status, "tt_mp2_energy_f32")
+    return energy, partials

@@ -1,0 +1,216 @@
+"""Contraction planner, drop-in for trntensor/plan.py.
+
+Host-side Python, as in the reference: subscript validation with the same
+error messages (trntensor/plan.py:68-113), a plan cache keyed by
+(subscripts, shapes, precision) (plan.py:116-185), the binary planner that
+recognises plain and batched matmuls (plan.py:261-314), greedy path search
+for 3+ operands (plan.py:188-243, same cost: product of the sizes of the
+pair's index union) and ``estimate_flops`` (plan.py:317-332, multiply-adds).
+
+``ContractionPlan.backend`` names the executor: ``"cuda"`` when a
+matmul/bmm plan's operands live on a CUDA device, else ``"pytorch"``.
+"""
+
+from __future__ import annotations
+
+import re
+from collections import Counter
+from dataclasses import dataclass, field
+
+import torch
+
+_PRECISIONS = ("fast", "kahan", "dd")
+_SUBSCRIPT_RE = re.compile(r"[a-zA-Z,]+(->[a-zA-Z]*)?")
+
+
+@dataclass
+class ContractionPlan:
+    """Execution plan for a tensor contraction (fields as in the reference)."""
+
+    subscripts: str
+    strategy: str  # "matmul" | "bmm" | "torch" | "path"
+    backend: str = "pytorch"  # "cuda" | "pytorch"
+    transA: bool = False
+    transB: bool = False
+    contraction_indices: list[str] = field(default_factory=list)
+    batch_indices: list[str] = field(default_factory=list)
+    output_indices: list[str] = field(default_factory=list)
+    estimated_flops: int = 0
+    contraction_path: list[tuple[int, int]] = field(default_factory=list)
+    precision: str = "fast"
+
+
+_PLAN_CACHE: dict[tuple, ContractionPlan] = {}
+
+
+def clear_plan_cache() -> None:
+    """Discard all cached contraction plans."""
+    _PLAN_CACHE.clear()
+
+
+def plan_cache_info() -> dict[str, int]:
+    """Cache statistics: ``{"size": number of cached plans}``."""
+    return {"size": len(_PLAN_CACHE)}
+
+
+def _check_precision(precision: str) -> None:
+    if precision not in _PRECISIONS:
+        raise ValueError(f"precision must be 'fast', 'kahan', or 'dd', got {precision!r}")
+    if precision == "dd":
+        raise NotImplementedError(
+            "precision='dd' (double-double accumulation) is not available; "
+            "use precision='kahan' (fp64 accumulation) as an alternative."
+        )
+
+
+def _parse_subscripts(subscripts: str) -> tuple[str, str]:
+    """Split 'ij,jk->ik' into ('ij,jk', 'ik'); implicit output = indices seen once, sorted."""
+    if "->" in subscripts:
+        lhs, rhs = subscripts.split("->")
+        return lhs, rhs
+    counts = Counter(c for c in subscripts if c.isalpha())
+    return subscripts, "".join(sorted(c for c, n in counts.items() if n == 1))
+
+
+def _validate_subscripts(subscripts: str, operands: tuple) -> None:
+    if not _SUBSCRIPT_RE.fullmatch(subscripts):
+        raise ValueError(
+            f"einsum subscript {subscripts!r} contains invalid characters; "
+            "only a-zA-Z, commas, and '->' are allowed"
+        )
+    lhs, _ = _parse_subscripts(subscripts)
+    terms = lhs.split(",")
+    if len(terms) != len(operands):
+        raise ValueError(
+            f"einsum subscript {subscripts!r} has {len(terms)} operand term(s) "
+            f"but {len(operands)} operand(s) were given"
+        )
+    seen: dict[str, tuple[int, int]] = {}
+    for k, (term, op) in enumerate(zip(terms, operands)):
+        if len(term) != op.ndim:
+            raise ValueError(
+                f"einsum operand {k} has shape {tuple(op.shape)} (ndim={op.ndim}) "
+                f"but subscript term {term!r} has {len(term)} indices"
+            )
+        for ch, n in zip(term, op.shape):
+            n = int(n)
+            if ch in seen and seen[ch][0] != n:
+                raise ValueError(
+                    f"einsum index {ch!r} is size {seen[ch][0]} in operand {seen[ch][1]} "
+                    f"but size {n} in operand {k}"
+                )
+            seen.setdefault(ch, (n, k))
+
+
+def _backend_for(strategy: str, operands: tuple) -> str:
+    if strategy in ("matmul", "bmm") and all(
+        isinstance(op, torch.Tensor) and op.device.type == "cuda" for op in operands
+    ):
+        from .dispatch import get_backend
+
+        return "cuda" if get_backend() in ("auto", "cuda") else "pytorch"
+    return "pytorch"
+
+
+def _plan_binary(subscripts: str, terms: list[str], out: str, operands: tuple) -> ContractionPlan:
+    a, b = terms
+    sa, sb, so = set(a), set(b), set(out)
+    contracted = sorted((sa & sb) - so)
+    batch = sorted(sa & sb & so)
+    A, B = operands
+    if len(contracted) == 1 and not batch and A.dim() == 2 and B.dim() == 2:
+        c = contracted[0]
+        return ContractionPlan(
+            subscripts=subscripts,
+            strategy="matmul",
+            transA=a.index(c) == 0,
+            transB=b.index(c) == 1,
+            contraction_indices=contracted,
+            output_indices=list(out),
+        )
+    if len(contracted) == 1 and len(batch) == 1 and A.dim() == 3 and B.dim() == 3:
+        return ContractionPlan(
+            subscripts=subscripts,
+            strategy="bmm",
+            contraction_indices=contracted,
+            batch_indices=batch,
+            output_indices=list(out),
+        )
+    return ContractionPlan(
+        subscripts=subscripts,
+        strategy="torch",
+        contraction_indices=contracted,
+        batch_indices=batch,
+        output_indices=list(out),
+    )
+
+
+def _greedy_path_search(
+    input_list: list[str], output_str: str, size_map: dict[str, int]
+) -> list[tuple[int, int]]:
+    """Greedy pairwise order (opt_einsum convention: indices into the current list).
+
+    Each step contracts the pair whose index union has the smallest product
+    of sizes; the intermediate keeps the indices still needed later, sorted.
+    """
+    ops = list(input_list)
+    path: list[tuple[int, int]] = []
+    while len(ops) > 2:
+        best = None
+        for x in range(len(ops)):
+            for y in range(x + 1, len(ops)):
+                keep = set(output_str).union(*(set(o) for k, o in enumerate(ops) if k not in (x, y)))
+                union = set(ops[x]) | set(ops[y])
+                cost = 1
+                for ch in union:
+                    cost *= size_map.get(ch, 1)
+                if best is None or cost < best[0]:
+                    best = (cost, x, y, union & keep)
+        _, x, y, inter = best
+        path.append((x, y))
+        ops = [o for k, o in enumerate(ops) if k not in (x, y)] + ["".join(sorted(inter))]
+    path.append((0, 1))
+    return path
+
+
+def plan_contraction(
+    subscripts: str, *operands: torch.Tensor, precision: str = "fast"
+) -> ContractionPlan:
+    """Plan a contraction; cached by (subscripts, operand shapes, precision)."""
+    _validate_subscripts(subscripts, operands)
+    if precision not in _PRECISIONS:
+        raise ValueError(f"precision must be 'fast', 'kahan', or 'dd', got {precision!r}")
+    key = (subscripts, tuple(tuple(op.shape) for op in operands), precision)
+    hit = _PLAN_CACHE.get(key)
+    if hit is not None:
+        return hit
+    lhs, out = _parse_subscripts(subscripts)
+    terms = lhs.split(",")
+    if len(operands) == 2:
+        plan = _plan_binary(subscripts, terms, out, operands)
+    elif len(operands) >= 3:
+        sizes = {ch: int(n) for t, op in zip(terms, operands) for ch, n in zip(t, op.shape)}
+        plan = ContractionPlan(
+            subscripts=subscripts,
+            strategy="path",
+            contraction_path=_greedy_path_search(terms, out, sizes),
+        )
+    else:
+        plan = ContractionPlan(subscripts=subscripts, strategy="torch")
+    plan.backend = _backend_for(plan.strategy, operands)
+    plan.precision = precision
+    _PLAN_CACHE[key] = plan
+    return plan
+
+
+def estimate_flops(subscripts: str, *operands: torch.Tensor) -> int:
+    """Multiply-add count: product of every distinct index's size."""
+    lhs, _ = _parse_subscripts(subscripts)
+    sizes: dict[str, int] = {}
+    for t, op in zip(lhs.split(","), operands):
+        for ch, n in zip(t, op.shape):
+            sizes[ch] = int(n)
+    total = 1
+    for ch in set(c for c in lhs if c.isalpha()):
+        total *= sizes.get(ch, 1)
+    return total

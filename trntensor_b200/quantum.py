@@ -1,0 +1,117 @@
+"""DF-MP2 primitives, drop-in for trntensor/quantum.py.
+
+Same signatures, validation and error messages as the reference
+(trntensor/quantum.py:21-84 and 103-185), plus an optional ``precision=``
+keyword with ``trntensor.einsum``'s meaning (trntensor/einsum.py:108-116):
+``"fast"`` computes in the input dtype (fp32 via 3xTF32 tensor cores),
+``"kahan"`` computes in fp64 and returns the input dtype, ``"dd"`` raises
+``NotImplementedError``.
+
+Unlike the reference there is no backend gate and no CPU fallback: both
+functions always run the sm_100a kernels, moving host tensors to the current
+CUDA device and returning results on the caller's device.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .dispatch import _cuda_mp2_energy
+from .plan import _check_precision
+
+
+def mp2_energy(
+    B: torch.Tensor,
+    eps_occ: torch.Tensor,
+    eps_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+) -> torch.Tensor:
+    """Second-order Møller–Plesset correlation energy, density-fitted.
+
+        E_MP2 = Σ_{ijab} T_{ijab} (2 T_{ijab} - T_{ijba}) / Δ_{ijab}
+        T_{ijab} = Σ_P B[i,a,P] B[j,b,P],  Δ_{ijab} = ε_i + ε_j - ε_a - ε_b
+
+    One fused device pass: T is accumulated in tensor memory and reduced in
+    the kernel epilogue; it never reaches HBM.
+
+    Parameters
+    ----------
+    B : (nocc, nvir, naux) tensor
+    eps_occ : (nocc,) tensor
+    eps_vir : (nvir,) tensor
+    precision : "fast" | "kahan"
+
+    Returns
+    -------
+    0-D tensor of ``B.dtype`` on ``B``'s device.
+    """
+    if B.dim() != 3:
+        raise ValueError(f"B must be 3D (nocc, nvir, naux); got shape {tuple(B.shape)}")
+    nocc, nvir, _naux = B.shape
+    if eps_occ.shape != (nocc,):
+        raise ValueError(f"eps_occ must have shape ({nocc},); got {tuple(eps_occ.shape)}")
+    if eps_vir.shape != (nvir,):
+        raise ValueError(f"eps_vir must have shape ({nvir},); got {tuple(eps_vir.shape)}")
+    _check_precision(precision)
+    if nocc == 0 or nvir == 0 or _naux == 0:
+        return B.new_zeros(())
+    energy, _ = _cuda_mp2_energy(B, eps_occ, eps_vir, precision=precision)
+    return energy.to(device=B.device, dtype=B.dtype)
+
+
+def mp2_pair_energies(
+    B: torch.Tensor,
+    eps_occ: torch.Tensor,
+    eps_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+) -> torch.Tensor:
+    """Per-pair energies E_ij as a (nocc, nocc) float64 tensor.
+
+    The same (nocc, nocc) partial the reference's device kernel returns before
+    its host-side sum (trntensor/nki/_kernels.py:152,205 and
+    trntensor/nki/dispatch.py:283); ``.sum()`` of it is ``mp2_energy``.
+    """
+    if B.dim() != 3:
+        raise ValueError(f"B must be 3D (nocc, nvir, naux); got shape {tuple(B.shape)}")
+    nocc, nvir, _naux = B.shape
+    if eps_occ.shape != (nocc,):
+        raise ValueError(f"eps_occ must have shape ({nocc},); got {tuple(eps_occ.shape)}")
+    if eps_vir.shape != (nvir,):
+        raise ValueError(f"eps_vir must have shape ({nvir},); got {tuple(eps_vir.shape)}")
+    _check_precision(precision)
+    _, partials = _cuda_mp2_energy(B, eps_occ, eps_vir, precision=precision, return_partials=True)
+    return partials.to(B.device)
+
+
+def ao_to_mo_transform(
+    eri: torch.Tensor,
+    C_occ: torch.Tensor,
+    C_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+) -> torch.Tensor:
+    """AO→MO transform B[i,a,P] = Σ_{μν} C_occ[μ,i] C_vir[ν,a] eri[μ,ν,P].
+
+    Two tensor-core GEMM phases ('mi,mnP->inP' then 'na,inP->iaP') with the
+    (i, ν, P) intermediate in an HBM workspace, as the reference's kernel does
+    (trntensor/nki/_kernels.py:209-296).
+    """
+    if eri.dim() != 3:
+        raise ValueError(f"eri must be 3D (nbasis, nbasis, naux); got shape {tuple(eri.shape)}")
+    nbasis_mu, nbasis_nu, _naux = eri.shape
+    if nbasis_mu != nbasis_nu:
+        raise ValueError(
+            f"eri first two dims must match (nbasis, nbasis); got ({nbasis_mu}, {nbasis_nu})"
+        )
+    nbasis = nbasis_mu
+    if C_occ.dim() != 2 or C_occ.shape[0] != nbasis:
+        raise ValueError(f"C_occ must have shape ({nbasis}, nocc); got {tuple(C_occ.shape)}")
+    if C_vir.dim() != 2 or C_vir.shape[0] != nbasis:
+        raise ValueError(f"C_vir must have shape ({nbasis}, nvir); got {tuple(C_vir.shape)}")
+    _check_precision(precision)
+    from .dispatch import _cuda_ao_to_mo_transform
+
+    out = _cuda_ao_to_mo_transform(eri, C_occ, C_vir, precision=precision)
+    return out.to(device=eri.device, dtype=eri.dtype)
