@@ -48,17 +48,14 @@ const char* tt_last_cuda_error(void);
 /* Number of unordered occupied pairs i <= j: nocc * (nocc + 1) / 2. */
 long long tt_mp2_num_pairs(int nocc);
 
-/* Workspace bytes tt_mp2_energy_f32 needs: hi and lo tf32 copies of B with
- * naux padded to a multiple of 16. */
+/* Workspace bytes tt_mp2_energy_f32 needs: three int8 slices of B (naux
+ * padded to a multiple of 64) plus one fp32 scale per (i, a) row. */
 size_t tt_mp2_workspace_bytes(int nocc, int nvir, int naux);
 
-/* Split x (rows x cols, row-major) into hi = tf32(x), lo = tf32(x - hi),
- * written as rows x cols_pad with zero padding (cols_pad >= cols, % 4 == 0). */
-int tt_split_tf32(const float* x, float* hi, float* lo, long long rows, int cols, int cols_pad,
-                  void* stream);
-
 /*
- * DF-MP2 correlation energy, fp32 inputs, 3xTF32 tcgen05 tensor cores.
+ * DF-MP2 correlation energy for fp32 inputs on int8 tensor cores (Ozaki
+ * scheme: each B row = power-of-two scale x three int8 slices; six exact
+ * int32-accumulated slice GEMMs per block; energy reduced in the epilogue).
  *   *energy = sum over the unordered pairs [pair_begin, pair_end) (linear
  *             id of (i, j), i <= j, row-major; the full sum is
  *             [0, tt_mp2_num_pairs(nocc))) of w_ij * E_ij, w = 2 for i < j,
@@ -74,12 +71,35 @@ int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir
                       void* workspace, size_t workspace_bytes, double* energy,
                       double* pair_partials, int* dev_status, void* stream);
 
-/* As tt_mp2_energy_f32, with B already split by tt_split_tf32 into
- * (nocc, nvir, naux_pad) hi/lo arrays (naux_pad % 16 == 0). */
-int tt_mp2_energy_presplit_f32(const float* B_hi, const float* B_lo, int naux_pad,
-                               const float* eps_occ, const float* eps_vir, int nocc, int nvir,
-                               long long pair_begin, long long pair_end, double* energy,
-                               double* pair_partials, int* dev_status, void* stream);
+/* Ozaki split of x (rows x cols, row-major fp32): per row a power-of-two
+ * scale[r] and three int8 slice planes q[t][r][0..cols_pad) (zero padded,
+ * cols_pad % 64 == 0) with x = scale * (q1 + q2/2^7 + q3/2^14) + O(2^-22 max). */
+int tt_split_i8(const float* x, signed char* q, float* scale, long long rows, int cols,
+                int cols_pad, void* stream);
+
+/* tt_mp2_energy_f32 on operands already split by tt_split_i8 with rows =
+ * nocc * nvir and cols_pad = naux_pad (lets callers reuse one split). */
+int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux_pad,
+                              const float* eps_occ, const float* eps_vir, int nocc, int nvir,
+                              long long pair_begin, long long pair_end, double* energy,
+                              double* pair_partials, int* dev_status, void* stream);
+
+/* Split x (rows x cols, row-major) into hi = tf32(x), lo = tf32(x - hi),
+ * written as rows x cols_pad with zero padding (cols_pad >= cols, % 4 == 0). */
+int tt_split_tf32(const float* x, float* hi, float* lo, long long rows, int cols, int cols_pad,
+                  void* stream);
+
+/* Bytes of hi + lo for tt_mp2_energy_tf32x3 (naux padded to 16). */
+size_t tt_mp2_tf32_workspace_bytes(int nocc, int nvir, int naux);
+
+/* Diagnostic: the same energy with 3xTF32 tcgen05 MMAs on tt_split_tf32
+ * operands (naux_pad % 16 == 0). The tensor core's fp32 accumulation rounds
+ * toward zero, so this variant is biased by ~2.4e-8 relative per 8 aux
+ * elements; it is kept to document that, not as a production path. */
+int tt_mp2_energy_tf32x3(const float* B_hi, const float* B_lo, int naux_pad,
+                         const float* eps_occ, const float* eps_vir, int nocc, int nvir,
+                         long long pair_begin, long long pair_end, double* energy,
+                         double* pair_partials, int* dev_status, void* stream);
 
 /* DF-MP2 energy in fp64 throughout (precision="kahan" semantics of
  * trntensor/einsum.py:108-111 applied to trntensor/quantum.py:87-100). */

@@ -193,7 +193,7 @@ class TestCAbi:
         lib = _lib.load()
         assert lib.tt_version() >= 100
         assert lib.tt_mp2_num_pairs(256) == 32896
-        assert lib.tt_mp2_workspace_bytes(2, 3, 5) == 2 * 2 * 3 * 16 * 4
+        assert lib.tt_mp2_workspace_bytes(2, 3, 5) == 1280 + 256  # 3 slices x 6 rows x 64, scales
         assert lib.tt_status_string(0) == b"ok"
         # argument checks happen before any CUDA call
         assert lib.tt_mp2_energy_f64(None, None, None, 1, 1, 1, 0, 1, None, None, None) == 1

@@ -90,32 +90,29 @@ def test_pair_ranges_add_up(cuda_ok):
 
 
 def test_capi_presplit_direct(cuda_ok):
-    """tt_split_tf32 + tt_mp2_energy_presplit_f32 through ctypes."""
+    """tt_split_i8 + tt_mp2_energy_presplit_i8 through ctypes."""
     lib = _lib.load()
     B, eo, ev = mp2_inputs(6, 130, 48, seed=5)
     Bd, eod, evd = B.cuda(), eo.cuda(), ev.cuda()
     nocc, nvir, naux = B.shape
-    pad = 48
-    hi = torch.empty(nocc, nvir, pad, device="cuda")
-    lo = torch.empty_like(hi)
+    pad = 64
+    q = torch.empty(3, nocc * nvir, pad, dtype=torch.int8, device="cuda")
+    sc = torch.empty(nocc * nvir, dtype=torch.float32, device="cuda")
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-    assert lib.tt_split_tf32(p(Bd), p(hi), p(lo), nocc * nvir, naux, pad, s) == 0
-    torch.cuda.synchronize()
-    torch.testing.assert_close(hi + lo, Bd, rtol=1e-6, atol=0)
-    assert (hi.view(torch.int32) & 0x1FFF).eq(0).all()
+    assert lib.tt_split_i8(p(Bd), p(q), p(sc), nocc * nvir, naux, pad, s) == 0
     energy = torch.empty((), dtype=torch.float64, device="cuda")
     status = torch.empty((), dtype=torch.int32, device="cuda")
-    st = lib.tt_mp2_energy_presplit_f32(p(hi), p(lo), pad, p(eod), p(evd), nocc, nvir, 0,
-                                        nocc * (nocc + 1) // 2, p(energy), None, p(status), s)
+    st = lib.tt_mp2_energy_presplit_i8(p(q), p(sc), pad, p(eod), p(evd), nocc, nvir, 0,
+                                       nocc * (nocc + 1) // 2, p(energy), None, p(status), s)
     assert st == 0
     torch.cuda.synchronize()
     assert status.item() == 0
     ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
     assert rel(energy.item(), ref) <= RTOL_F32
     # bad arguments are rejected before launch
-    assert lib.tt_mp2_energy_presplit_f32(p(hi), p(lo), 40, p(eod), p(evd), nocc, nvir, 0, 1,
-                                          p(energy), None, p(status), s) == 2
+    assert lib.tt_mp2_energy_presplit_i8(p(q), p(sc), 40, p(eod), p(evd), nocc, nvir, 0, 1,
+                                         p(energy), None, p(status), s) == 2
 
 
 def test_config2_against_oracle(cuda_ok):
@@ -153,3 +150,38 @@ def test_config4_sampled_pairs(cuda_ok):
         ref = oracle.mp2_pair_energy(Bc, eoc, evc, i, j, np.float64)
         _, part = _cuda_mp2_energy(B, eo, ev, pair_range=(pid, pid + 1), return_partials=True)
         assert rel(part[i, j].item(), ref) <= 1e-6
+
+
+def test_ozaki_split_is_exact_to_21_bits(cuda_ok):
+    """tt_split_i8: x == s (q1 + q2/2^7 + q3/2^14) up to half a unit of the last slice."""
+    lib = _lib.load()
+    B, _, _ = mp2_inputs(3, 50, 100, seed=9)
+    rows, cols, pad = 150, 100, 128
+    Bd = B.cuda().reshape(rows, cols)
+    q = torch.empty(3, rows, pad, dtype=torch.int8, device="cuda")
+    s = torch.empty(rows, dtype=torch.float32, device="cuda")
+    st = lib.tt_split_i8(ctypes.c_void_p(Bd.data_ptr()), ctypes.c_void_p(q.data_ptr()),
+                         ctypes.c_void_p(s.data_ptr()), rows, cols, pad,
+                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 0
+    torch.cuda.synchronize()
+    qd = q.double()
+    rec = s.double()[:, None] * (qd[0] + qd[1] / 128 + qd[2] / 16384)
+    err = (rec[:, :cols] - Bd.double()).abs()
+    assert (err <= 0.5 * s.double()[:, None] / 16384 * 1.0001).all()
+    assert (q[:, :, cols:] == 0).all()
+    assert (q[0].abs() <= 127).all() and (q[1].abs() <= 64).all() and (q[2].abs() <= 64).all()
+    # scales are powers of two
+    m, e = torch.frexp(s)
+    assert (m == 0.5).all()
+
+
+def test_tf32x3_diagnostic_is_biased(cuda_ok):
+    """The 3xTF32 tensor-core variant loses ~2e-8 relative per 8 aux elements
+    (fp32 accumulation rounds toward zero); the int8 path does not."""
+    B, eo, ev = mp2_inputs(4, 256, 2048, seed=1, device="cuda")
+    e64, _ = _cuda_mp2_energy(B.double(), eo.double(), ev.double())
+    e_tf, _ = _cuda_mp2_energy(B, eo, ev, kernel="tf32x3")
+    e_i8, _ = _cuda_mp2_energy(B, eo, ev)
+    assert rel(e_tf.item(), e64.item()) > 5e-6
+    assert rel(e_i8.item(), e64.item()) < RTOL_F32

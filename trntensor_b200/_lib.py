@@ -37,9 +37,12 @@ SIGNATURES: dict[str, tuple] = {
     "tt_last_cuda_error": (ctypes.c_char_p, []),
     "tt_mp2_num_pairs": (_LL, [_I]),
     "tt_mp2_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "tt_mp2_tf32_workspace_bytes": (_SZ, [_I, _I, _I]),
     "tt_split_tf32": (_I, [_P, _P, _P, _LL, _I, _I, _P]),
+    "tt_split_i8": (_I, [_P, _P, _P, _LL, _I, _I, _P]),
     "tt_mp2_energy_f32": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _SZ, _P, _P, _P, _P]),
-    "tt_mp2_energy_presplit_f32": (_I, [_P, _P, _I, _P, _P, _I, _I, _LL, _LL, _P, _P, _P, _P]),
+    "tt_mp2_energy_presplit_i8": (_I, [_P, _P, _I, _P, _P, _I, _I, _LL, _LL, _P, _P, _P, _P]),
+    "tt_mp2_energy_tf32x3": (_I, [_P, _P, _I, _P, _P, _I, _I, _LL, _LL, _P, _P, _P, _P]),
     "tt_mp2_energy_f64": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _P, _P]),
     "tt_mp2_energy_simt_f32": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _P, _P]),
 }

@@ -1,6 +1,8 @@
-// C-ABI entry points for the DF-MP2 energy (tensor-core 3xTF32, fp64 and
-// fp32 CUDA-core variants) and the tf32 hi/lo split.
+// C-ABI entry points for the DF-MP2 energy: int8 Ozaki tensor-core kernel
+// (the fp32 path), the 3xTF32 tensor-core kernel (kept as a diagnostic),
+// fp64 and fp32 CUDA-core kernels, and the operand splits they consume.
 #include "common.cuh"
+#include "mp2_i8.cuh"
 #include "mp2_simt.cuh"
 #include "mp2_tf32.cuh"
 
@@ -44,6 +46,9 @@ int mp2_setup(int dev) {
     if (cudaFuncSetAttribute(mp2::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              mp2::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
+    if (cudaFuncSetAttribute(mp2tf::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mp2tf::kSmemBytes) != cudaSuccess)
+      return TT_ERR_CUDA;
     if (cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev) !=
         cudaSuccess)
       return TT_ERR_CUDA;
@@ -51,7 +56,9 @@ int mp2_setup(int dev) {
   });
 }
 
-inline int naux_padded(int naux) { return (naux + 15) / 16 * 16; }
+inline int naux_padded(int naux) { return (naux + 15) / 16 * 16; }     // tf32 split
+inline int naux_padded_i8(int naux) { return (naux + 63) / 64 * 64; }  // int8 slices
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 int check_pairs(int nocc, long long pb, long long pe) {
   const long long np = (long long)nocc * (nocc + 1) / 2;
@@ -83,7 +90,82 @@ long long tt_mp2_num_pairs(int nocc) {
 
 size_t tt_mp2_workspace_bytes(int nocc, int nvir, int naux) {
   if (nocc <= 0 || nvir <= 0 || naux <= 0) return 0;
+  const size_t rows = (size_t)nocc * (size_t)nvir;
+  return align256(3ull * rows * (size_t)naux_padded_i8(naux)) + align256(rows * sizeof(float));
+}
+
+size_t tt_mp2_tf32_workspace_bytes(int nocc, int nvir, int naux) {
+  if (nocc <= 0 || nvir <= 0 || naux <= 0) return 0;
   return 2ull * (size_t)nocc * (size_t)nvir * (size_t)naux_padded(naux) * sizeof(float);
+}
+
+int tt_split_i8(const float* x, signed char* q, float* scale, long long rows, int cols,
+                int cols_pad, void* stream) {
+  if (!x || !q || !scale) return TT_ERR_NULL;
+  if (rows < 0 || cols <= 0 || cols_pad < cols || cols_pad % 64 != 0) return TT_ERR_SHAPE;
+  if (!aligned16(q)) return TT_ERR_ALIGN;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = mp2_setup(dev);
+  if (st != TT_OK) return st;
+  if (rows == 0) return TT_OK;
+  long long blocks = (rows + 7) / 8;
+  const long long cap = (long long)g_num_sms[dev] * 16;
+  if (blocks > cap) blocks = cap;
+  mp2::split_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      x, reinterpret_cast<int8_t*>(q), scale, rows, cols, cols_pad);
+  return cuda_status(cudaGetLastError());
+}
+
+int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux_pad,
+                              const float* eps_occ, const float* eps_vir, int nocc, int nvir,
+                              long long pair_begin, long long pair_end, double* energy,
+                              double* pair_partials, int* dev_status, void* stream) {
+  if (!Q || !scale || !eps_occ || !eps_vir || !energy || !dev_status) return TT_ERR_NULL;
+  if (nocc <= 0 || nvir <= 0 || naux_pad <= 0 || naux_pad % 64 != 0) return TT_ERR_SHAPE;
+  if (nocc > 65535 || nvir > 65535) return TT_ERR_SHAPE;
+  if (check_pairs(nocc, pair_begin, pair_end) != TT_OK) return TT_ERR_SHAPE;
+  if (!aligned16(Q)) return TT_ERR_ALIGN;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = mp2_setup(dev);
+  if (st != TT_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  TT_CUDA(cudaMemsetAsync(energy, 0, sizeof(double), s));
+  TT_CUDA(cudaMemsetAsync(dev_status, 0, sizeof(int), s));
+  if (pair_partials)
+    TT_CUDA(cudaMemsetAsync(pair_partials, 0, sizeof(double) * (size_t)nocc * nocc, s));
+  if (pair_end == pair_begin) return TT_OK;
+  // Slices as a 4-D byte tensor (aux, vir, occ, slice), innermost first;
+  // one box = 64 aux x 128 rows x all 3 slices, 64B swizzle.
+  CUtensorMap mq;
+  const uint64_t rows = (uint64_t)nocc * nvir;
+  const uint64_t dims[4] = {(uint64_t)naux_pad, (uint64_t)nvir, (uint64_t)nocc, 3};
+  const uint64_t strides[3] = {(uint64_t)naux_pad, (uint64_t)naux_pad * nvir,
+                               (uint64_t)naux_pad * rows};
+  const uint32_t box[4] = {(uint32_t)mp2::kKC, (uint32_t)mp2::kBlk, 1, 3};
+  if (encode_tmap(&mq, Q, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_DATA_TYPE_UINT8))
+    return TT_ERR_TMA;
+  mp2::Params p;
+  p.scale = scale;
+  p.eps_occ = eps_occ;
+  p.eps_vir = eps_vir;
+  p.nocc = nocc;
+  p.nvir = nvir;
+  p.naux_pad = naux_pad;
+  p.pair_begin = pair_begin;
+  p.pair_end = pair_end;
+  p.nblk = (nvir + mp2::kBlk - 1) / mp2::kBlk;
+  p.energy = energy;
+  p.pair_partials = pair_partials;
+  p.err = dev_status;
+  const long long n_items = (pair_end - pair_begin) * (long long)(p.nblk * (p.nblk + 1) / 2);
+  const int grid = (int)(n_items < g_num_sms[dev] ? n_items : g_num_sms[dev]);
+  mp2::energy_kernel<<<grid, mp2::kThreads, mp2::kSmemBytes, s>>>(mq, p);
+  return cuda_status(cudaGetLastError());
 }
 
 int tt_split_tf32(const float* x, float* hi, float* lo, long long rows, int cols, int cols_pad,
@@ -99,7 +181,7 @@ int tt_split_tf32(const float* x, float* hi, float* lo, long long rows, int cols
   return launch_split(x, hi, lo, rows, cols, cols_pad, (cudaStream_t)stream, g_num_sms[dev]);
 }
 
-int tt_mp2_energy_presplit_f32(const float* B_hi, const float* B_lo, int naux_pad,
+int tt_mp2_energy_tf32x3(const float* B_hi, const float* B_lo, int naux_pad,
                                const float* eps_occ, const float* eps_vir, int nocc, int nvir,
                                long long pair_begin, long long pair_end, double* energy,
                                double* pair_partials, int* dev_status, void* stream) {
@@ -125,15 +207,15 @@ int tt_mp2_energy_presplit_f32(const float* B_hi, const float* B_lo, int naux_pa
   CUtensorMap mA_hi, mA_lo, mB_hi, mB_lo;
   const uint64_t dims[3] = {(uint64_t)naux_pad, (uint64_t)nvir, (uint64_t)nocc};
   const uint64_t strides[2] = {(uint64_t)naux_pad * 4, (uint64_t)naux_pad * 4 * nvir};
-  const uint32_t boxA[3] = {(uint32_t)mp2::kKC, (uint32_t)mp2::kM, 1};
-  const uint32_t boxB[3] = {(uint32_t)mp2::kKC, (uint32_t)mp2::kN, 1};
+  const uint32_t boxA[3] = {(uint32_t)mp2tf::kKC, (uint32_t)mp2tf::kM, 1};
+  const uint32_t boxB[3] = {(uint32_t)mp2tf::kKC, (uint32_t)mp2tf::kN, 1};
   if (encode_tmap(&mA_hi, B_hi, 3, dims, strides, boxA, CU_TENSOR_MAP_SWIZZLE_64B) ||
       encode_tmap(&mA_lo, B_lo, 3, dims, strides, boxA, CU_TENSOR_MAP_SWIZZLE_64B) ||
       encode_tmap(&mB_hi, B_hi, 3, dims, strides, boxB, CU_TENSOR_MAP_SWIZZLE_64B) ||
       encode_tmap(&mB_lo, B_lo, 3, dims, strides, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
     return TT_ERR_TMA;
 
-  mp2::Params p;
+  mp2tf::Params p;
   p.eps_occ = eps_occ;
   p.eps_vir = eps_vir;
   p.nocc = nocc;
@@ -141,13 +223,13 @@ int tt_mp2_energy_presplit_f32(const float* B_hi, const float* B_lo, int naux_pa
   p.naux_pad = naux_pad;
   p.pair_begin = pair_begin;
   p.pair_end = pair_end;
-  p.n_rects = mp2::rect_count(nvir);
+  p.n_rects = mp2tf::rect_count(nvir);
   p.energy = energy;
   p.pair_partials = pair_partials;
   p.err = dev_status;
   const long long n_items = (pair_end - pair_begin) * (long long)p.n_rects;
   const int grid = (int)(n_items < g_num_sms[dev] ? n_items : g_num_sms[dev]);
-  mp2::energy_kernel<<<grid, mp2::kThreads, mp2::kSmemBytes, s>>>(mA_hi, mA_lo, mB_hi, mB_lo, p);
+  mp2tf::energy_kernel<<<grid, mp2tf::kThreads, mp2tf::kSmemBytes, s>>>(mA_hi, mA_lo, mB_hi, mB_lo, p);
   return cuda_status(cudaGetLastError());
 }
 
@@ -162,13 +244,15 @@ int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir
   const size_t need = tt_mp2_workspace_bytes(nocc, nvir, naux);
   if (workspace_bytes < need) return TT_ERR_WORKSPACE;
   if (!aligned16(workspace)) return TT_ERR_ALIGN;
-  const int naux_pad = naux_padded(naux);
-  float* hi = static_cast<float*>(workspace);
-  float* lo = hi + (size_t)nocc * nvir * naux_pad;
-  int st = tt_split_tf32(B, hi, lo, (long long)nocc * nvir, naux, naux_pad, stream);
+  const int naux_pad = naux_padded_i8(naux);
+  const size_t rows = (size_t)nocc * nvir;
+  signed char* q = static_cast<signed char*>(workspace);
+  float* scale = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                          align256(3ull * rows * (size_t)naux_pad));
+  int st = tt_split_i8(B, q, scale, (long long)rows, naux, naux_pad, stream);
   if (st != TT_OK) return st;
-  return tt_mp2_energy_presplit_f32(hi, lo, naux_pad, eps_occ, eps_vir, nocc, nvir, pair_begin,
-                                    pair_end, energy, pair_partials, dev_status, stream);
+  return tt_mp2_energy_presplit_i8(q, scale, naux_pad, eps_occ, eps_vir, nocc, nvir, pair_begin,
+                                   pair_end, energy, pair_partials, dev_status, stream);
 }
 
 }  // extern "C"

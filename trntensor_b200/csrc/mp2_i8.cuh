@@ -1,0 +1,363 @@
+// DF-MP2 pair-energy contraction on tcgen05 int8 tensor cores (Ozaki scheme).
+//
+// Math (the reference's trntensor/quantum.py:87-100; device kernel
+// trntensor/nki/_kernels.py:119-207):
+//   E = sum_{i,j} sum_{a,b} T_ab (2 T_ab - T_ba) / (e_i + e_j - e_a - e_b),
+//   T = B_i . B_j^T   (B_i = B[i], nvir x naux, aux fastest).
+//
+// Why int8: tcgen05's fp32 accumulation of tf32 products rounds toward
+// zero, so a K = 6144 contraction in 3xTF32 comes out biased by ~1e-4
+// (measured), far outside the 1e-6 energy tolerance. Integer MMAs
+// accumulate exactly. Each B row r = (i, a) is written as
+//     B[r, P] = s_r * (q1 + q2 / 2^7 + q3 / 2^14)[r, P] + O(s_r 2^-15),
+// s_r a power of two, q_t int8 ("slices", Ozaki et al. error-free
+// splitting with a per-row exponent), and
+//     T_ab = s_a s_b (L2 + L3 / 2^7 + L4 / 2^14),
+//     L2 = Q1.Q1^T, L3 = Q1.Q2^T + Q2.Q1^T, L4 = Q1.Q3^T + Q2.Q2^T + Q3.Q1^T
+// are six exact int8 GEMMs accumulated in int32 TMEM columns (one column
+// block per level). Dropped terms are O(2^-21) relative and unbiased.
+//
+// Work decomposition: unordered occupied pairs i <= j (E_ij == E_ji, weight
+// 2 for i < j), square 128 x 128 virtual blocks A <= B covering the upper
+// triangle a <= b. Per (pair, block) a CTA runs two phases over the full aux
+// range: x = T[A,B] (operands B_i[A], B_j[B]), whose fp32 value is parked in
+// TMEM columns 384..511, then y = (T[B,A])^T (operands B_j[A], B_i[B]), so
+// that T_ab and its exchange partner T_ba share a TMEM lane and column. The
+// epilogue adds the (a,b) and (b,a) terms: x(2x-y) + y(2y-x), weight 1 for
+// a < b, 1/2 for a == b, 0 for a > b.
+//
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer, warps 2..9 = epilogue (lane quarter = warp % 4, column half =
+// (warp - 2) / 4).
+#pragma once
+#include "ptx.cuh"
+
+namespace tt {
+namespace mp2 {
+
+constexpr int kBlk = 128;                 // virtual block edge (M = N = 128)
+constexpr int kKC = 64;                   // aux elements (bytes) per stage
+constexpr int kSlices = 3;
+constexpr int kStages = 4;
+constexpr int kSliceTile = kBlk * kKC;    // 8 KB
+constexpr int kOperandBytes = kSlices * kSliceTile;  // 24 KB
+constexpr int kStageBytes = 2 * kOperandBytes;       // A and B: 48 KB
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+constexpr int kColStash = 3 * kBlk;       // TMEM column of the parked x
+
+struct Params {
+  const float* scale;    // (nocc, nvir) power-of-two row scales s_r
+  const float* eps_occ;
+  const float* eps_vir;
+  int nocc, nvir, naux_pad;
+  long long pair_begin, pair_end;
+  int nblk;              // ceil(nvir / 128)
+  double* energy;
+  double* pair_partials;
+  int* err;
+};
+
+__host__ __device__ inline long long pair_offset(long long i, long long n) {
+  return i * n - i * (i - 1) / 2;
+}
+__device__ inline void pair_decode(long long p, int n, int& i, int& j) {
+  double nn = 2.0 * n + 1.0;
+  long long ii = (long long)((nn - sqrt(nn * nn - 8.0 * (double)p)) * 0.5);
+  if (ii < 0) ii = 0;
+  if (ii > n - 1) ii = n - 1;
+  while (ii > 0 && pair_offset(ii, n) > p) --ii;
+  while (ii + 1 < n && pair_offset(ii + 1, n) <= p) ++ii;
+  i = (int)ii;
+  j = (int)(ii + (p - pair_offset(ii, n)));
+}
+
+struct Item {
+  int i, j, a0, b0;
+};
+__device__ inline Item item_decode(long long w, const Params& p) {
+  const int nbp = p.nblk * (p.nblk + 1) / 2;
+  Item it;
+  pair_decode(p.pair_begin + w / nbp, p.nocc, it.i, it.j);
+  int r = (int)(w % nbp), A = 0;
+  while (r >= p.nblk - A) {
+    r -= p.nblk - A;
+    ++A;
+  }
+  it.a0 = A * kBlk;
+  it.b0 = (A + r) * kBlk;
+  return it;
+}
+
+__device__ __forceinline__ float level_combine(int l2, int l3, int l4) {
+  return (float)l2 + (float)l3 * (1.0f / 128.0f) + (float)l4 * (1.0f / 16384.0f);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    energy_kernel(const __grid_constant__ CUtensorMap mapQ, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* final_bar = acc_empty + 1;
+  uint32_t* tmem_slot = (uint32_t*)(final_bar + 1);
+  double* red = (double*)(tmem_slot + 2);  // kEpiWarps doubles
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nbp = p.nblk * (p.nblk + 1) / 2;
+  const long long n_items = (p.pair_end - p.pair_begin) * (long long)nbp;
+  const int nkc = p.naux_pad / kKC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 32 * kEpiWarps);
+    mbar_init(final_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&mapQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+        const Item t = item_decode(w, p);
+        for (int ph = 0; ph < 2 && ok; ++ph) {
+          const int occA = ph == 0 ? t.i : t.j;
+          const int occB = ph == 0 ? t.j : t.i;
+          for (int kc = 0; kc < nkc; ++kc, ++it) {
+            const int s = it % kStages;
+            if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = smem + s * kStageBytes;
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_4d(st, &mapQ, &full[s], kc * kKC, t.a0, occA, 0);
+            tma_load_4d(st + kOperandBytes, &mapQ, &full[s], kc * kKC, t.b0, occB, 0);
+          }
+        }
+      }
+      const uint32_t issued = it;
+      for (uint32_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k)
+        mbar_wait_drain(&full[k % kStages], (k / kStages) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8(kBlk, kBlk, 0, 0);
+      uint32_t it = 0, round = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+        for (int ph = 0; ph < 2 && ok; ++ph, ++round) {
+          if (!mbar_wait(acc_empty, (round & 1u) ^ 1u, p.err, kDevTimeoutAccFree)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int kc = 0; kc < nkc; ++kc, ++it) {
+            const int s = it % kStages;
+            if (!mbar_wait(&full[s], (it / kStages) & 1u, p.err, kDevTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + s * kStageBytes);
+            const uint32_t sb = sa + kOperandBytes;
+#pragma unroll
+            for (int ks = 0; ks < kKC / 32; ++ks) {
+              uint64_t a[3], b[3];
+#pragma unroll
+              for (int t = 0; t < 3; ++t) {
+                a[t] = smem_desc(sa + t * kSliceTile + ks * 32, 16, 512, 4);
+                b[t] = smem_desc(sb + t * kSliceTile + ks * 32, 16, 512, 4);
+              }
+              const uint32_t first = (kc | ks) != 0;
+              mma_i8(tmem + 0 * kBlk, a[0], b[0], idesc, first);
+              mma_i8(tmem + 1 * kBlk, a[0], b[1], idesc, first);
+              mma_i8(tmem + 2 * kBlk, a[0], b[2], idesc, first);
+              mma_i8(tmem + 1 * kBlk, a[1], b[0], idesc, 1);
+              mma_i8(tmem + 2 * kBlk, a[1], b[1], idesc, 1);
+              mma_i8(tmem + 2 * kBlk, a[2], b[0], idesc, 1);
+            }
+            mma_commit(&empty[s]);
+          }
+          if (ok) mma_commit(acc_full);
+        }
+      }
+      mma_commit(final_bar);
+      mbar_wait_drain(final_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int q = warp & 3;            // TMEM lane quarter
+    const int c0 = (ew >> 2) * (kBlk / 2);  // this warp's 64-column half
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    double my_energy = 0.0;
+    uint32_t round = 0;
+    for (long long w = blockIdx.x; w < n_items; w += gridDim.x) {
+      const Item t = item_decode(w, p);
+      const int a = t.a0 + row;
+      const bool arow = a < p.nvir;
+      // ---- phase x: park s_ia s_jb (L2 + L3/2^7 + L4/2^14) in the stash columns
+      if (!mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)) break;
+      tc_fence_after();
+      {
+        const float sa = arow ? __ldg(p.scale + (long long)t.i * p.nvir + a) : 0.f;
+        for (int c = c0; c < c0 + kBlk / 2; c += 16) {
+          int l2[16], l3[16], l4[16];
+          tmem_ld16i(lane_base + 0 * kBlk + c, l2);
+          tmem_ld16i(lane_base + 1 * kBlk + c, l3);
+          tmem_ld16i(lane_base + 2 * kBlk + c, l4);
+          tmem_ld_wait();
+          float x[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int b = t.b0 + c + k;
+            const float sb = b < p.nvir ? __ldg(p.scale + (long long)t.j * p.nvir + b) : 0.f;
+            x[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
+          }
+          tmem_st16(lane_base + kColStash + c, x);
+        }
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      ++round;
+      // ---- phase y: combine with the parked x and reduce the energy
+      if (!mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)) break;
+      tc_fence_after();
+      double acc = 0.0;
+      {
+        const float sa = arow ? __ldg(p.scale + (long long)t.j * p.nvir + a) : 0.f;
+        const float eija = arow ? (__ldg(p.eps_occ + t.i) + __ldg(p.eps_occ + t.j)) -
+                                      __ldg(p.eps_vir + a)
+                                : 0.f;
+        for (int c = c0; c < c0 + kBlk / 2; c += 16) {
+          int l2[16], l3[16], l4[16];
+          float x[16];
+          tmem_ld16i(lane_base + 0 * kBlk + c, l2);
+          tmem_ld16i(lane_base + 1 * kBlk + c, l3);
+          tmem_ld16i(lane_base + 2 * kBlk + c, l4);
+          tmem_ld16(lane_base + kColStash + c, x);
+          tmem_ld_wait();
+          float part = 0.f;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int b = t.b0 + c + k;
+            if (arow && b < p.nvir && a <= b) {
+              const float sb = __ldg(p.scale + (long long)t.i * p.nvir + b);
+              const float y = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
+              const float xv = x[k];
+              const float den = eija - __ldg(p.eps_vir + b);
+              float v = 2.f * (xv * xv - xv * y + y * y) / den;
+              if (a == b) v *= 0.5f;
+              part += v;
+            }
+          }
+          acc += (double)part;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      ++round;
+      const double wgt = (t.i == t.j) ? 1.0 : 2.0;
+      my_energy += wgt * acc;
+      if (p.pair_partials != nullptr) {
+        double s = acc;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) {
+          atomicAdd(p.pair_partials + (long long)t.i * p.nocc + t.j, s);
+          if (t.i != t.j) atomicAdd(p.pair_partials + (long long)t.j * p.nocc + t.i, s);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) my_energy += __shfl_xor_sync(0xffffffffu, my_energy, o);
+    if (lane == 0) red[ew] = my_energy;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int k = 0; k < kEpiWarps; ++k) tot += red[k];
+    if (tot != 0.0) atomicAdd(p.energy, tot);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Ozaki split of one row per warp: s = 2^(e-7) with max|x| * 2^(7-e) <= 127,
+// q1 = rint(x/s), q2 = rint((x/s - q1) 2^7), q3 = rint(((x/s - q1) 2^7 - q2) 2^7).
+// Every step is exact in fp32 (power-of-two scaling, Sterbenz subtraction).
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
+
+__global__ void split_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+                             float* __restrict__ scale, long long rows, int cols, int cols_pad) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long plane = rows * (long long)cols_pad;
+  for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += warps) {
+    const float* xr = x + r * cols;
+    float m = 0.f;
+    for (int c = lane; c < cols; c += 32) m = fmaxf(m, fabsf(__ldg(xr + c)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int e = 0;
+    float inv = 0.f, s = 0.f;
+    if (m > 0.f && m < 3.0e38f && m > 1.0e-30f) {
+      e = ilogbf(m) + 1;  // m < 2^e
+      if (m * pow2f(7 - e) > 127.f) ++e;
+      inv = pow2f(7 - e);
+      s = pow2f(e - 7);
+    }
+    if (lane == 0) scale[r] = s;
+    int8_t* q1 = q + r * cols_pad;
+    int8_t* q2 = q1 + plane;
+    int8_t* q3 = q2 + plane;
+    for (int c = lane * 4; c < cols_pad; c += 128) {
+      uint32_t w1 = 0, w2 = 0, w3 = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float v = (c + k < cols) ? __ldg(xr + c + k) * inv : 0.f;
+        const float d1 = rintf(v);
+        const float r1 = (v - d1) * 128.f;
+        const float d2 = rintf(r1);
+        const float r2 = (r1 - d2) * 128.f;
+        const float d3 = rintf(r2);
+        w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * k);
+        w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * k);
+        w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * k);
+      }
+      *reinterpret_cast<uint32_t*>(q1 + c) = w1;
+      *reinterpret_cast<uint32_t*>(q2 + c) = w2;
+      *reinterpret_cast<uint32_t*>(q3 + c) = w3;
+    }
+  }
+}
+
+}  // namespace mp2
+}  // namespace tt

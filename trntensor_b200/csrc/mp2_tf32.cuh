@@ -26,7 +26,7 @@
 #include "ptx.cuh"
 
 namespace tt {
-namespace mp2 {
+namespace mp2tf {
 
 constexpr int kM = 128;               // rows per rectangle (block A)
 constexpr int kN = 256;               // columns per rectangle (block B)
@@ -278,5 +278,5 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-}  // namespace mp2
+}  // namespace mp2tf
 }  // namespace tt

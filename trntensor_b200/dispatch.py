@@ -123,8 +123,9 @@ def _cuda_mp2_energy(
 
     Returns ``(energy_fp64_device_scalar, partials_or_None)``; both stay on the
     device. ``pair_range`` selects a half-open range of unordered pair ids
-    (i <= j, row-major) for sharding. ``kernel="simt"`` selects the CUDA-core
-    fp32 cross-check kernel instead of the tensor-core one.
+    (i <= j, row-major) for sharding. ``kernel`` picks the fp32 kernel:
+    ``"tc"`` (int8 Ozaki tensor cores, the product path), ``"simt"`` (CUDA-core
+    fp32 cross-check) or ``"tf32x3"`` (biased 3xTF32 diagnostic).
     """
     lib = _lib.load()
     dev = _device()
@@ -153,6 +154,20 @@ def _cuda_mp2_energy(
             _ptr(energy), _ptr(partials), stream,
         )
         _lib.check(st, "tt_mp2_energy_simt_f32")
+        return energy, partials
+    if kernel == "tf32x3":
+        pad = (naux + 15) // 16 * 16
+        hi = torch.empty((nocc, nvir, pad), dtype=torch.float32, device=dev)
+        lo = torch.empty_like(hi)
+        dev_status = torch.empty((), dtype=torch.int32, device=dev)
+        _lib.check(lib.tt_split_tf32(_ptr(Bd), _ptr(hi), _ptr(lo), nocc * nvir, naux, pad, stream),
+                   "tt_split_tf32")
+        st = lib.tt_mp2_energy_tf32x3(
+            _ptr(hi), _ptr(lo), pad, _ptr(eo), _ptr(ev), nocc, nvir, pb, pe,
+            _ptr(energy), _ptr(partials), _ptr(dev_status), stream,
+        )
+        _lib.check(st, "tt_mp2_energy_tf32x3")
+        _check_status(dev_status, "tt_mp2_energy_tf32x3")
         return energy, partials
     ws_bytes = int(lib.tt_mp2_workspace_bytes(nocc, nvir, naux))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
