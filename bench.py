@@ -1,0 +1,506 @@
+#!/usr/bin/env python
+"""DF-MP2 pair-contraction throughput on B200.
+
+One "step" is one full DF-MP2 energy evaluation of config 4
+(nocc=256, nvir=1792, naux=6144, fp32 inputs, seeded synthetic data):
+Ozaki int8 split of B + the fused pair-energy kernel over the step's
+unordered pairs (+ one fp64 NCCL all-reduce when N > 1). Work is fixed
+as N grows (strong scaling); ranks split the pairs.
+
+Metric: algorithmic fp32-equivalent TFLOP/s = unique pairs x 2 nvir^2 naux
+per step / step time (max over ranks).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the reference's CPU algorithm (the numpy port in
+oracle/, the reference being pure Python/torch) on host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+CONFIGS = {
+    4: dict(nocc=256, nvir=1792, naux=6144),
+    2: dict(nocc=64, nvir=448, naux=1536),
+    0: dict(nocc=8, nvir=32, naux=96),
+}
+METRIC = "DF-MP2 pair-contraction TFLOP/s"
+# dram__bytes_read.sum + dram__bytes_write.sum of one mp2::energy_kernel launch,
+# from the ncu capture in profiles/mp2_energy_kernel_config4.md, scaled by pairs.
+TRAFFIC_BYTES_PER_LAUNCH = 3.80e12  # 61.1 GB per 528 pairs (ncu, nocc=32) x 32896/528
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=4)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--nocc", type=int, default=None,
+                    help="override nocc (same tile shapes, fewer pairs; for profiling captures)")
+    args = ap.parse_args()
+    if args.nocc is not None:
+        CONFIGS[args.config] = dict(CONFIGS[args.config], nocc=args.nocc)
+    return args
+
+
+def flops_per_pair(c):
+    return 2.0 * c["nvir"] ** 2 * c["naux"]
+
+
+def unique_pairs(c):
+    return c["nocc"] * (c["nocc"] + 1) // 2
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def _target(self):
+        try:
+            props = torch.cuda.get_device_properties(self.dev)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            return ["-i", bus]
+        except Exception:
+            return ["-i", str(self.dev)]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", *self._target(), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.rows.append([x.strip() for x in line.split(",")])
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                pw.append(float(r[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "power_w_max": max(pw) if pw else None,
+            "samples": len(sm),
+            "reasons": sorted(reasons),
+        }
+
+
+# ---------------------------------------------------------- distributed
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        backend = "nccl" if args.impl == "ours" else "gloo"
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend=backend)
+    elif args.impl == "ours":
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+# ------------------------------------------------------------- CPU arms
+def _blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_pair_sample(c, seconds, B_rows=None, seed=0):
+    """Time the oracle port of the reference's loop body on sampled ordered pairs.
+
+    Returns (seconds per ordered pair, pairs timed). ``B_rows(i)`` gives
+    B[i] as a numpy (nvir, naux) fp32 array.
+    """
+    import numpy as np
+
+    from oracle import oracle
+
+    nocc, nvir, naux = c["nocc"], c["nvir"], c["naux"]
+    rng = np.random.default_rng(seed)
+    g = torch.Generator().manual_seed(seed)
+    eo = (torch.rand(nocc, generator=g, dtype=torch.float64) * 1.5 - 2.0).float().numpy()
+    ev = (torch.rand(nvir, generator=g, dtype=torch.float64) * 2.8 + 0.2).float().numpy()
+    cache: dict[int, np.ndarray] = {}
+
+    def rows(i):
+        if i not in cache:
+            if B_rows is not None:
+                cache[i] = B_rows(i)
+            else:
+                gi = torch.Generator().manual_seed(seed * 100003 + i)
+                cache[i] = (torch.randn(nvir, naux, generator=gi) / math.sqrt(naux)).numpy()
+        return cache[i]
+
+    occ = rng.choice(nocc, size=min(nocc, 8), replace=False)
+    pairs = [(int(a), int(b)) for a in occ for b in occ]
+    rng.shuffle(pairs)
+    Bsub = np.zeros((nocc, 1, 1), dtype=np.float32)  # placeholder for shape only
+    del Bsub
+    # warm-up one pair (BLAS thread pool start-up)
+    i0, j0 = pairs[0]
+    Bij = np.stack([rows(i0), rows(j0)])
+    oracle.mp2_pair_energy(Bij, eo[[i0, j0]], ev, 0, 1)
+    times = []
+    t_end = time.perf_counter() + seconds
+    for i, j in pairs:
+        Bij = np.stack([rows(i), rows(j)])
+        t0 = time.perf_counter()
+        oracle.mp2_pair_energy(Bij, eo[[i, j]], ev, 0, 1)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and len(times) >= 4:
+            break
+    return statistics.mean(times), len(times)
+
+
+def cpu_metric(c, t_pair):
+    """Whole-job TFLOP/s of the reference algorithm (all nocc^2 ordered pairs)."""
+    t_job = c["nocc"] ** 2 * t_pair
+    return unique_pairs(c) * flops_per_pair(c) / t_job / 1e12, t_job
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    c = CONFIGS[args.config]
+    for _ in range(args.warmup):
+        cpu_pair_sample(c, 0.0, seed=1)
+    vals, secs = [], []
+    per_step_seconds = max(1.0, args.cpu_seconds / max(1, args.steps))
+    npairs_total = 0
+    for k in range(args.steps):
+        t0 = time.perf_counter()
+        t_pair, n = cpu_pair_sample(c, per_step_seconds, seed=2 + k)
+        secs.append(time.perf_counter() - t0)
+        npairs_total += n
+        vals.append(cpu_metric(c, t_pair)[0])
+    value = statistics.mean(vals)
+    cores = _blas_threads()
+    sample = (f"{npairs_total} ordered (i,j) pairs of config {args.config} over {args.steps} steps "
+              f"(reference loop body, fp32, numpy BLAS); extrapolated to all nocc^2 ordered pairs")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * statistics.mean(secs),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": {"workload": f"mp2_config{args.config}", **c, "sampled": True},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- our arm
+def measure_int8_peak(device) -> float | None:
+    """Dense int8 GEMM TOPS via torch._int_mm (cuBLASLt), best of 10."""
+    try:
+        n = 8192
+        a = torch.randint(-100, 100, (n, n), dtype=torch.int8, device=device)
+        b = torch.randint(-100, 100, (n, n), dtype=torch.int8, device=device).t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = float("inf")
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch._int_mm(a, b)
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e) / 1e3)
+        del a, b
+        return 2.0 * n**3 / best / 1e12
+    except Exception:
+        return None
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            pass
+    return {}
+
+
+def run_ours(args, rank, world, local):
+    import trntensor_b200 as tt
+    from trntensor_b200 import _lib, distributed
+    from trntensor_b200.dispatch import _cuda_mp2_energy
+    from trntensor_b200.inputs import mp2_inputs
+
+    lib = _lib.load()
+    dev = torch.device("cuda", local)
+    c = CONFIGS[args.config]
+    nocc, nvir, naux = c["nocc"], c["nvir"], c["naux"]
+    npairs = unique_pairs(c)
+    pb, pe = distributed.pair_range(npairs, rank, world)
+    my_flops = (pe - pb) * flops_per_pair(c)
+    job_flops = npairs * flops_per_pair(c)
+
+    B, eo, ev = mp2_inputs(nocc, nvir, naux, seed=0, dtype=torch.float32, device=dev)
+    naux_pad = (naux + 63) // 64 * 64
+    rows = nocc * nvir
+    q = torch.empty(3, rows, naux_pad, dtype=torch.int8, device=dev)
+    sc = torch.empty(rows, dtype=torch.float32, device=dev)
+    energy = torch.empty((), dtype=torch.float64, device=dev)
+    status = torch.empty((), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step(k_events=None):
+        _lib.check(lib.tt_split_i8(P(B), P(q), P(sc), rows, naux, naux_pad, sp), "split")
+        if k_events is not None:
+            k_events[0].record(stream)
+        _lib.check(lib.tt_mp2_energy_presplit_i8(P(q), P(sc), naux_pad, P(eo), P(ev), nocc, nvir,
+                                                 pb, pe, P(energy), None, P(status), sp), "energy")
+        if k_events is not None:
+            k_events[1].record(stream)
+        if world > 1:
+            dist.all_reduce(energy, op=dist.ReduceOp.SUM)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status 0x{int(status.item()):x} during warm-up")
+
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(kev[k])
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clk = clocks.stop()
+    elapsed = t_start.elapsed_time(t_end) / 1e3
+    elapsed = max_over_ranks(elapsed, world, dev)
+    kernel_s = statistics.mean(a.elapsed_time(b) / 1e3 for a, b in kev)
+    kernel_s = max_over_ranks(kernel_s, world, dev)
+    energy_value = float(energy.item())
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status 0x{int(status.item()):x} in the timed region")
+
+    value = args.steps * job_flops / elapsed / 1e12
+
+    # sanity check: 8 pairs against the fp64 CUDA-core kernel
+    e_chk, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(pb, min(pe, pb + 8)))
+    e_ref, _ = _cuda_mp2_energy(B.double(), eo.double(), ev.double(), pair_range=(pb, min(pe, pb + 8)))
+    check_rel = abs(e_chk.item() - e_ref.item()) / abs(e_ref.item())
+
+    # roofline of the dominant kernel
+    int8_peak = measure_int8_peak(dev)
+    peaks = measured_peaks()
+    bf16 = peaks.get("bf16_tflops")
+    if int8_peak is not None:
+        peak_src = "int8 dense GEMM measured in this run (torch._int_mm, cuBLASLt, 8192^3, best of 10) / 6"
+        peak_eff = int8_peak / 6.0
+    else:
+        int8_peak = 2.0 * (bf16 or 1590.0)
+        peak_src = "2 x bf16 dense (MEASURED_PEAKS.json) / 6"
+        peak_eff = int8_peak / 6.0
+    achieved = my_flops / kernel_s / 1e12
+    roof = {
+        "bound": "tensor",
+        "achieved": achieved,
+        "peak": peak_eff,
+        "unit": "TFLOP/s",
+        "frac": achieved / peak_eff,
+        "traffic": TRAFFIC_BYTES_PER_LAUNCH,
+        "kernel": "tt::mp2::energy_kernel",
+        "kernel_ms": kernel_s * 1e3,
+        "peak_source": peak_src,
+        "int8_tops_peak": int8_peak,
+        "int8_tops_achieved": 6.0 * achieved,
+        "flops_per_launch": my_flops,
+        "flops_convention": "unique pairs i<=j x 2 nvir^2 naux (fp32-equivalent); the kernel runs 6 int8 slice GEMMs per fp32 GEMM",
+    }
+    if bf16:
+        roof["north_star_3xtf32_peak"] = bf16 / 2.0 / 3.0
+        roof["north_star_frac"] = achieved / (bf16 / 2.0 / 3.0)
+
+    # end-to-end: public API, host (pinned) inputs, result back on the host
+    e2e = None
+    if not args.no_e2e:
+        Bh = B.cpu().pin_memory()
+        eoh, evh = eo.cpu(), ev.cpu()
+        del q
+        api = tt.mp2_energy if world == 1 else distributed.mp2_energy
+        api(Bh, eoh, evh)  # warm-up (allocator, workspace)
+        torch.cuda.synchronize(dev)
+        ts = []
+        for _ in range(args.e2e_steps):
+            barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            e_host = api(Bh, eoh, evh)
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b) / 1e3)
+        t_e2e = max_over_ranks(statistics.mean(ts), world, dev)
+        h2d = (Bh.numel() + eoh.numel() + evh.numel()) * 4 * world
+        e2e = {"value": job_flops / t_e2e / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": 8 * world, "ms_per_step": t_e2e * 1e3,
+               "api": "trntensor_b200.mp2_energy" if world == 1 else
+                      "trntensor_b200.distributed.mp2_energy",
+               "energy": float(e_host.item())}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        Bc = B.cpu()
+        t_pair, n = cpu_pair_sample(c, args.cpu_seconds, B_rows=lambda i: Bc[i].numpy())
+        v, t_job = cpu_metric(c, t_pair)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": _blas_threads(), "kind": "port",
+               "sample": f"{n} ordered (i,j) pairs of config {args.config} timed with the numpy "
+                         f"port of the reference loop body (fp32); extrapolated to all "
+                         f"{nocc}^2 ordered pairs = {t_job:.0f} s",
+               "host_cpus": os.cpu_count()}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "arith": "int8 Ozaki slices (3), int32 tensor-core accumulation, fp32/fp64 epilogue",
+            "data": "synthetic (seeded on device, BASELINE config distributions)",
+            "config": {"workload": f"mp2_config{args.config}", "nocc": nocc, "nvir": nvir,
+                       "naux": naux, "unique_pairs": npairs, "flops_per_step": job_flops,
+                       "l2": "inputs larger than L2 (B 11.3 GB fp32, slices 8.5 GB)",
+                       "parallelism": f"pairs sharded over {world} GPU(s), B replicated, "
+                                      f"fp64 all-reduce"},
+            "energy": energy_value,
+            "check": {"pairs": 8, "rel_err_vs_fp64_kernel": check_rel},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = init_dist(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

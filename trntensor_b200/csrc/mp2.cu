@@ -82,6 +82,10 @@ int launch_split(const float* x, float* hi, float* lo, long long rows, int cols,
 
 using namespace tt;
 
+// Debug hook: per-CTA wait-cycle counters of TT_MP2_PROFILE builds.
+static long long* g_mp2_prof = nullptr;
+extern "C" void tt_debug_set_profile_buffer(long long* buf) { g_mp2_prof = buf; }
+
 extern "C" {
 
 long long tt_mp2_num_pairs(int nocc) {
@@ -162,6 +166,7 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
   p.energy = energy;
   p.pair_partials = pair_partials;
   p.err = dev_status;
+  p.prof = g_mp2_prof;
   const long long n_items = (pair_end - pair_begin) * (long long)(p.nblk * (p.nblk + 1) / 2);
   const int grid = (int)(n_items < g_num_sms[dev] ? n_items : g_num_sms[dev]);
   mp2::energy_kernel<<<grid, mp2::kThreads, mp2::kSmemBytes, s>>>(mq, p);

@@ -57,6 +57,7 @@ struct Params {
   double* energy;
   double* pair_partials;
   int* err;
+  long long* prof;  // optional per-CTA wait-cycle counters (TT_MP2_PROFILE builds)
 };
 
 __host__ __device__ inline long long pair_offset(long long i, long long n) {
@@ -163,20 +164,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_s8(kBlk, kBlk, 0, 0);
       uint32_t it = 0, round = 0;
+#ifdef TT_MP2_PROFILE
+      long long wait_acc = 0, wait_full = 0;
+      const long long t_begin = clock64();
+#endif
       bool ok = true;
       for (long long w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
         for (int ph = 0; ph < 2 && ok; ++ph, ++round) {
+#ifdef TT_MP2_PROFILE
+          long long t0 = clock64();
+#endif
           if (!mbar_wait(acc_empty, (round & 1u) ^ 1u, p.err, kDevTimeoutAccFree)) {
             ok = false;
             break;
           }
+#ifdef TT_MP2_PROFILE
+          wait_acc += clock64() - t0;
+#endif
           tc_fence_after();
           for (int kc = 0; kc < nkc; ++kc, ++it) {
             const int s = it % kStages;
+#ifdef TT_MP2_PROFILE
+            long long t1 = clock64();
+#endif
             if (!mbar_wait(&full[s], (it / kStages) & 1u, p.err, kDevTimeoutFull)) {
               ok = false;
               break;
             }
+#ifdef TT_MP2_PROFILE
+            wait_full += clock64() - t1;
+#endif
             tc_fence_after();
             const uint32_t sa = smem_u32(smem + s * kStageBytes);
             const uint32_t sb = sa + kOperandBytes;
@@ -189,11 +206,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 b[t] = smem_desc(sb + t * kSliceTile + ks * 32, 16, 512, 4);
               }
               const uint32_t first = (kc | ks) != 0;
+              // Grouped by A slice so that each A slice is read from shared
+              // memory once per 32-wide k-step (collector buffer reuse).
+#ifndef TT_MP2_NO_COLLECTOR
+              mma_i8_fill(tmem + 0 * kBlk, a[0], b[0], idesc, first);
+              mma_i8_use(tmem + 1 * kBlk, a[0], b[1], idesc, first);
+              mma_i8_lastuse(tmem + 2 * kBlk, a[0], b[2], idesc, first);
+              mma_i8_fill(tmem + 1 * kBlk, a[1], b[0], idesc, 1);
+              mma_i8_lastuse(tmem + 2 * kBlk, a[1], b[1], idesc, 1);
+#else
               mma_i8(tmem + 0 * kBlk, a[0], b[0], idesc, first);
               mma_i8(tmem + 1 * kBlk, a[0], b[1], idesc, first);
               mma_i8(tmem + 2 * kBlk, a[0], b[2], idesc, first);
               mma_i8(tmem + 1 * kBlk, a[1], b[0], idesc, 1);
               mma_i8(tmem + 2 * kBlk, a[1], b[1], idesc, 1);
+#endif
               mma_i8(tmem + 2 * kBlk, a[2], b[0], idesc, 1);
             }
             mma_commit(&empty[s]);
@@ -203,6 +230,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(final_bar);
       mbar_wait_drain(final_bar, 0);
+#ifdef TT_MP2_PROFILE
+      if (p.prof) {
+        p.prof[blockIdx.x * 4 + 0] = clock64() - t_begin;
+        p.prof[blockIdx.x * 4 + 1] = wait_full;
+        p.prof[blockIdx.x * 4 + 2] = wait_acc;
+      }
+#endif
     }
   } else {
     // ------------------------------------------------------------ epilogue

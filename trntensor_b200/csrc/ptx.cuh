@@ -143,6 +143,25 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// kind::i8 MMA using the A-operand collector buffer: Op is one of
+// "fill" (read A from shared memory and keep it), "use" (reuse the kept A),
+// "lastuse" (reuse it one last time). Consecutive MMAs that share A then
+// read it from shared memory once.
+#define TT_MMA_I8_COLLECTOR(NAME, OP)                                                    \
+  __device__ __forceinline__ void NAME(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,  \
+                                       uint32_t idesc, uint32_t accumulate) {            \
+    asm volatile(                                                                        \
+        "{\n\t.reg .pred p;\n\t"                                                         \
+        "setp.ne.b32 p, %4, 0;\n\t"                                                      \
+        "tcgen05.mma.cta_group::1.kind::i8.collector::a::" OP " [%0], %1, %2, %3, p;\n\t}" \
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)              \
+        : "memory");                                                                     \
+  }
+TT_MMA_I8_COLLECTOR(mma_i8_fill, "fill")
+TT_MMA_I8_COLLECTOR(mma_i8_use, "use")
+TT_MMA_I8_COLLECTOR(mma_i8_lastuse, "lastuse")
+#undef TT_MMA_I8_COLLECTOR
+
 // Arrive on an mbarrier once every MMA issued so far by this thread is done.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(

@@ -1,0 +1,70 @@
+"""Multi-GPU DF-MP2 and AO->MO: one process per GPU over torch.distributed.
+
+* ``mp2_energy``: B is replicated on every rank; the unordered occupied
+  pairs (i <= j, row-major linear ids) are split into equal contiguous
+  ranges, each rank runs the fused kernel on its range, and one fp64 scalar
+  is summed across ranks (NCCL all-reduce on GPUs, gloo on CPU).
+* ``ao_to_mo_transform``: each rank transforms its own slab of the
+  auxiliary index P; there is no communication. ``aux_slab`` gives the slab.
+
+The reference has no multi-device code; this module is B200-specific.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .dispatch import _cuda_mp2_energy
+
+
+def _world(group=None) -> tuple[int, int]:
+    if not (dist.is_available() and dist.is_initialized()):
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def pair_range(npairs: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous, balanced share [begin, end) of ``npairs`` for ``rank``."""
+    base, rem = divmod(npairs, world)
+    begin = rank * base + min(rank, rem)
+    return begin, begin + base + (1 if rank < rem else 0)
+
+
+def aux_slab(naux: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous share [p0, p1) of the auxiliary index for ``rank``."""
+    return pair_range(naux, rank, world)
+
+
+def reduce_energy(local: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum a 0-D fp64 tensor over the group (in place) and return it."""
+    _, world = _world(group)
+    if world > 1:
+        dist.all_reduce(local, op=dist.ReduceOp.SUM, group=group)
+    return local
+
+
+def mp2_energy(
+    B: torch.Tensor,
+    eps_occ: torch.Tensor,
+    eps_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+    group=None,
+) -> torch.Tensor:
+    """DF-MP2 energy with the pairs sharded over the process group.
+
+    Every rank passes the full (replicated) inputs and gets the full energy
+    back, as a 0-D tensor of ``B.dtype`` on ``B``'s device.
+    """
+    from .quantum import _validate_mp2
+
+    _validate_mp2(B, eps_occ, eps_vir, precision)
+    rank, world = _world(group)
+    nocc = int(B.shape[0])
+    npairs = nocc * (nocc + 1) // 2
+    e, _ = _cuda_mp2_energy(
+        B, eps_occ, eps_vir, precision=precision, pair_range=pair_range(npairs, rank, world)
+    )
+    reduce_energy(e, group)
+    return e.to(device=B.device, dtype=B.dtype)

@@ -20,6 +20,18 @@ from .dispatch import _cuda_mp2_energy
 from .plan import _check_precision
 
 
+def _validate_mp2(B, eps_occ, eps_vir, precision):
+    """Checks and messages of trntensor/quantum.py:58-64, plus ``precision``."""
+    if B.dim() != 3:
+        raise ValueError(f"B must be 3D (nocc, nvir, naux); got shape {tuple(B.shape)}")
+    nocc, nvir, _naux = B.shape
+    if eps_occ.shape != (nocc,):
+        raise ValueError(f"eps_occ must have shape ({nocc},); got {tuple(eps_occ.shape)}")
+    if eps_vir.shape != (nvir,):
+        raise ValueError(f"eps_vir must have shape ({nvir},); got {tuple(eps_vir.shape)}")
+    _check_precision(precision)
+
+
 def mp2_energy(
     B: torch.Tensor,
     eps_occ: torch.Tensor,
@@ -46,14 +58,8 @@ def mp2_energy(
     -------
     0-D tensor of ``B.dtype`` on ``B``'s device.
     """
-    if B.dim() != 3:
-        raise ValueError(f"B must be 3D (nocc, nvir, naux); got shape {tuple(B.shape)}")
+    _validate_mp2(B, eps_occ, eps_vir, precision)
     nocc, nvir, _naux = B.shape
-    if eps_occ.shape != (nocc,):
-        raise ValueError(f"eps_occ must have shape ({nocc},); got {tuple(eps_occ.shape)}")
-    if eps_vir.shape != (nvir,):
-        raise ValueError(f"eps_vir must have shape ({nvir},); got {tuple(eps_vir.shape)}")
-    _check_precision(precision)
     if nocc == 0 or nvir == 0 or _naux == 0:
         return B.new_zeros(())
     energy, _ = _cuda_mp2_energy(B, eps_occ, eps_vir, precision=precision)
@@ -73,14 +79,7 @@ def mp2_pair_energies(
     its host-side sum (trntensor/nki/_kernels.py:152,205 and
     trntensor/nki/dispatch.py:283); ``.sum()`` of it is ``mp2_energy``.
     """
-    if B.dim() != 3:
-        raise ValueError(f"B must be 3D (nocc, nvir, naux); got shape {tuple(B.shape)}")
-    nocc, nvir, _naux = B.shape
-    if eps_occ.shape != (nocc,):
-        raise ValueError(f"eps_occ must have shape ({nocc},); got {tuple(eps_occ.shape)}")
-    if eps_vir.shape != (nvir,):
-        raise ValueError(f"eps_vir must have shape ({nvir},); got {tuple(eps_vir.shape)}")
-    _check_precision(precision)
+    _validate_mp2(B, eps_occ, eps_vir, precision)
     _, partials = _cuda_mp2_energy(B, eps_occ, eps_vir, precision=precision, return_partials=True)
     return partials.to(B.device)
 
