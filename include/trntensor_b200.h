@@ -101,6 +101,27 @@ int tt_mp2_energy_tf32x3(const float* B_hi, const float* B_lo, int naux_pad,
                          long long pair_begin, long long pair_end, double* energy,
                          double* pair_partials, int* dev_status, void* stream);
 
+/* Scratch size of tt_mp2_energy_f32_noalloc (64 MiB of device memory that
+ * every GPU using the library keeps until the process exits). */
+#define TT_MP2_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/*
+ * tt_mp2_energy_f32 for callers that cannot allocate device memory (host
+ * programs that own the whole HBM budget, pipelines that cannot afford
+ * cudaMalloc's device-wide synchronisation, FFI callers with no allocator).
+ * No counterpart in the reference. Computes the full energy (all pairs)
+ * using a fixed scratch array inside the library instead of a workspace:
+ * problems with tt_mp2_workspace_bytes(nocc, nvir, naux) >
+ * TT_MP2_NOALLOC_SCRATCH_BYTES are rejected with TT_ERR_WORKSPACE. Calls no
+ * allocation routine. All calls share the one scratch array: calls that
+ * overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. The first call on a device looks up the
+ * scratch's device address; make it before any stream capture.
+ */
+int tt_mp2_energy_f32_noalloc(const float* B, const float* eps_occ, const float* eps_vir,
+                              int nocc, int nvir, int naux, double* energy,
+                              double* pair_partials, int* dev_status, void* stream);
+
 /* DF-MP2 energy in fp64 throughout (precision="kahan" semantics of
  * trntensor/einsum.py:108-111 applied to trntensor/quantum.py:87-100). */
 int tt_mp2_energy_f64(const double* B, const double* eps_occ, const double* eps_vir, int nocc,

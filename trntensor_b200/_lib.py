@@ -42,6 +42,7 @@ SIGNATURES: dict[str, tuple] = {
     "tt_split_i8": (_I, [_P, _P, _P, _LL, _I, _I, _P]),
     "tt_mp2_energy_f32": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _SZ, _P, _P, _P, _P]),
     "tt_mp2_energy_presplit_i8": (_I, [_P, _P, _I, _P, _P, _I, _I, _LL, _LL, _P, _P, _P, _P]),
+    "tt_mp2_energy_f32_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "tt_mp2_energy_tf32x3": (_I, [_P, _P, _I, _P, _P, _I, _I, _LL, _LL, _P, _P, _P, _P]),
     "tt_mp2_energy_f64": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _P, _P]),
     "tt_mp2_energy_simt_f32": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _P, _P]),
