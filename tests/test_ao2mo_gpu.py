@@ -1,0 +1,92 @@
+"""AO->MO transform on the GPU against the reference's numbers.
+
+Tolerance (north star): transformed tensors max-relative 1e-5 in fp32 and
+1e-12 in fp64, where max-relative = max|B - B_ref| / max|B_ref|.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import trntensor_b200 as tt
+from oracle import oracle
+from tests.helpers import AO_CASES, ao_case_inputs
+from trntensor_b200.inputs import ao2mo_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 1e-5
+TOL_F64 = 1e-12
+
+
+def max_rel(b, ref):
+    b = np.asarray(b, dtype=np.float64)
+    return np.abs(b - ref).max() / np.abs(ref).max()
+
+
+@pytest.mark.parametrize("name", sorted(AO_CASES))
+def test_fp32_and_fp64_match_reference(golden, cuda_ok, name):
+    eri, co, cv = ao_case_inputs(golden, name)[:3]
+    B32 = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda())
+    assert B32.dtype == torch.float32 and B32.device.type == "cuda"
+    B64 = tt.ao_to_mo_transform(eri.double().cuda(), co.double().cuda(), cv.double().cuda())
+    Bk = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda(), precision="kahan")
+    assert Bk.dtype == torch.float32
+    if f"{name}/B_fp64" in golden:
+        ref = golden[f"{name}/B_fp64"]
+        assert max_rel(B32.cpu().numpy(), ref) <= TOL_F32
+        assert max_rel(B64.cpu().numpy(), ref) <= TOL_F64
+        assert max_rel(Bk.cpu().numpy(), ref) <= 1e-7
+    else:
+        idx = golden[f"{name}/B_fp64_sample_idx"]
+        ref = golden[f"{name}/B_fp64_sample"]
+        for B, tol in ((B32, TOL_F32), (B64, TOL_F64)):
+            got = B.cpu().double().flatten().numpy()[idx]
+            assert np.abs(got - ref).max() / np.abs(ref).max() <= tol
+
+
+@pytest.mark.parametrize("name", ["ao_kat_compose", "ao_kat_pipeline"])
+def test_pipeline_energy(golden, cuda_ok, name):
+    """AO -> MO -> E on the device (tests/test_nki_kernels.py:178-196, 242-258)."""
+    eri, co, cv, eo, ev = ao_case_inputs(golden, name)
+    B = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda())
+    e = tt.mp2_energy(B, eo.cuda(), ev.cuda())
+    ref = float(golden[f"{name}/e_fp64"])
+    assert abs(e.item() - ref) / abs(ref) <= 1e-5
+    B64 = tt.ao_to_mo_transform(eri.double(), co.double(), cv.double())
+    e64 = tt.mp2_energy(B64, eo.double(), ev.double())
+    assert abs(e64.item() - ref) / abs(ref) <= 1e-11
+
+
+def test_host_round_trip(golden, cuda_ok):
+    eri, co, cv = ao_case_inputs(golden, "ao_kat_small")
+    B = tt.ao_to_mo_transform(eri, co, cv)
+    assert B.device.type == "cpu" and B.shape == (3, 5, 12)
+
+
+def test_config1_against_oracle(cuda_ok):
+    eri, co, cv = ao2mo_inputs(128, 16, 112, 384, seed=0)
+    ref, _ = oracle.ao_to_mo_two_step(eri.double().numpy(), co.double().numpy(),
+                                      cv.double().numpy())
+    B = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda())
+    assert max_rel(B.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_config3_p_slab(cuda_ok):
+    """BASELINE config 3 (nbf 1024, nocc 128, nvir 896, naux 3072): full-size
+    transform on the GPU; the transform is independent per P, so a 16-wide
+    P slab is checked against the fp64 CPU oracle and against the GPU fp64
+    path."""
+    nbf, nocc, nvir, naux = 1024, 128, 896, 3072
+    eri, co, cv = ao2mo_inputs(nbf, nocc, nvir, naux, seed=3, device="cuda")
+    B = tt.ao_to_mo_transform(eri, co, cv)
+    assert B.shape == (nocc, nvir, naux)
+    for p0 in (0, 1500, naux - 16):
+        slab = eri[:, :, p0:p0 + 16].double().cpu().numpy()
+        ref, _ = oracle.ao_to_mo_two_step(slab, co.double().cpu().numpy(),
+                                          cv.double().cpu().numpy())
+        assert max_rel(B[:, :, p0:p0 + 16].cpu().numpy(), ref) <= TOL_F32
+        B64 = tt.ao_to_mo_transform(eri[:, :, p0:p0 + 16].double(), co.double(), cv.double())
+        assert max_rel(B64.cpu().numpy(), ref) <= TOL_F64

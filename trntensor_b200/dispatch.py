@@ -179,3 +179,36 @@ def _cuda_mp2_energy(
     _lib.check(st, "tt_mp2_energy_f32")
     _check_status(dev_status, "tt_mp2_energy_f32")
     return energy, partials
+
+
+def _cuda_ao_to_mo_transform(
+    eri: torch.Tensor,
+    C_occ: torch.Tensor,
+    C_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+) -> torch.Tensor:
+    """AO->MO transform on the current CUDA device; result stays on the device.
+
+    fp32 inputs compute in fp32, float64 inputs or ``precision="kahan"`` in
+    fp64 (trntensor/einsum.py:108-111 semantics: the caller casts back).
+    """
+    lib = _lib.load()
+    dev = _device()
+    cdt = torch.float64 if (precision == "kahan" or eri.dtype == torch.float64) else torch.float32
+    nbf, _, naux = (int(s) for s in eri.shape)
+    nocc, nvir = int(C_occ.shape[1]), int(C_vir.shape[1])
+    out = torch.zeros((nocc, nvir, naux), dtype=cdt, device=dev)
+    if out.numel() == 0 or nbf == 0:
+        return out
+    e = _to_dev(eri, dev, cdt)
+    co = _to_dev(C_occ, dev, cdt)
+    cv = _to_dev(C_vir, dev, cdt)
+    esz = 8 if cdt == torch.float64 else 4
+    ws_bytes = int(lib.tt_ao2mo_workspace_bytes(nbf, nocc, nvir, naux, esz))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    fn = lib.tt_ao2mo_f64 if cdt == torch.float64 else lib.tt_ao2mo_f32
+    st = fn(_ptr(e), _ptr(co), _ptr(cv), nbf, nocc, nvir, naux, _ptr(ws), ws_bytes, _ptr(out),
+            ctypes.c_void_p(_stream_handle()))
+    _lib.check(st, "tt_ao2mo")
+    return out
