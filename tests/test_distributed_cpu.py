@@ -1,0 +1,101 @@
+"""Multi-rank host logic on CPU with gloo (world size 2 and 4): pair and aux
+partitioning, the fp64 scalar all-reduce, and a rank that fails before the
+collective (the others get an error instead of hanging)."""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from trntensor_b200 import distributed
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_pair_range_partition():
+    for n in (1, 36, 2080, 32896, 7):
+        for w in (1, 2, 3, 4, 8):
+            rs = [distributed.pair_range(n, r, w) for r in range(w)]
+            assert rs[0][0] == 0 and rs[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(rs, rs[1:]))
+            sizes = [e - b for b, e in rs]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def _worker(rank, world, port, mode, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        from datetime import timedelta
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+        if mode == "reduce":
+            nocc = 9
+            npairs = nocc * (nocc + 1) // 2
+            b, e = distributed.pair_range(npairs, rank, world)
+            # stand-in for the kernel: each pair id contributes (id + 1)
+            local = torch.tensor(float(sum(range(b + 1, e + 1))), dtype=torch.float64)
+            distributed.reduce_energy(local)
+            q.put((rank, local.item(), npairs * (npairs + 1) / 2))
+        elif mode == "slabs":
+            naux = 10
+            B = torch.arange(3 * 4 * naux, dtype=torch.float32).reshape(3, 4, naux)
+            p0, p1 = distributed.aux_slab(naux, rank, world)
+            full = distributed.gather_aux(B[:, :, p0:p1].contiguous(), naux)
+            q.put((rank, bool(torch.equal(full, B)), True))
+        elif mode == "fail":
+            if rank == 1:
+                raise RuntimeError("injected failure on rank 1 before the all-reduce")
+            t = torch.ones((), dtype=torch.float64)
+            try:
+                dist.all_reduce(t)
+                q.put((rank, "no error", "error"))
+            except Exception as exc:  # the collective times out / aborts
+                q.put((rank, "error", "error"))
+        dist.destroy_process_group()
+    except RuntimeError as exc:
+        if "injected" in str(exc):
+            q.put((rank, "raised", "raised"))
+        else:
+            q.put((rank, traceback.format_exc(), None))
+
+
+def _run(world, mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=90) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_energy_all_reduce(world):
+    for rank, got, want in _run(world, "reduce"):
+        assert got == want, (rank, got)
+
+
+def test_aux_slabs_reassemble():
+    for rank, ok, want in _run(2, "slabs"):
+        assert ok is want, (rank, ok)
+
+
+def test_failed_rank_does_not_hang_the_others():
+    res = dict((r, g) for r, g, _ in _run(2, "fail"))
+    assert res[1] == "raised"
+    assert res[0] == "error"

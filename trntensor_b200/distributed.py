@@ -68,3 +68,38 @@ def mp2_energy(
     )
     reduce_energy(e, group)
     return e.to(device=B.device, dtype=B.dtype)
+
+
+def ao_to_mo_transform(
+    eri: torch.Tensor,
+    C_occ: torch.Tensor,
+    C_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+    group=None,
+    sharded_input: bool = False,
+) -> torch.Tensor:
+    """AO->MO transform of this rank's slab of the auxiliary index.
+
+    With ``sharded_input=False`` every rank passes the full eri and transforms
+    ``eri[:, :, p0:p1]`` (its ``aux_slab``); with ``sharded_input=True`` eri is
+    already the rank's contiguous slab. Returns the rank's (nocc, nvir, p1-p0)
+    block of B. There is no communication.
+    """
+    from .quantum import ao_to_mo_transform as _single
+
+    rank, world = _world(group)
+    if not sharded_input:
+        p0, p1 = aux_slab(int(eri.shape[2]), rank, world)
+        eri = eri[:, :, p0:p1].contiguous()
+    return _single(eri, C_occ, C_vir, precision=precision)
+
+
+def gather_aux(local: torch.Tensor, naux: int, group=None) -> torch.Tensor:
+    """Reassemble the full (nocc, nvir, naux) B from every rank's slab."""
+    rank, world = _world(group)
+    if world == 1:
+        return local
+    parts = [None] * world
+    dist.all_gather_object(parts, local.cpu(), group=group)
+    return torch.cat(parts, dim=2).to(local.device)
