@@ -59,6 +59,7 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-ao2mo", action="store_true", help="skip the AO->MO config 3 leg")
     ap.add_argument("--nocc", type=int, default=None,
                     help="override nocc (same tile shapes, fewer pairs; for profiling captures)")
     args = ap.parse_args()
@@ -317,6 +318,74 @@ def measured_peaks():
     return {}
 
 
+AO_CONFIG = dict(nbf=1024, nocc=128, nvir=896, naux=3072)
+
+
+def measure_ao2mo(args, rank, world, local):
+    """AO->MO config 3 transform time, aux index sharded over the ranks.
+
+    Each rank transforms its contiguous (nbf, nbf, naux/N) slab (sliced out
+    before timing), inputs resident; ms = max over ranks of the mean step.
+    """
+    from trntensor_b200 import _lib, distributed
+    from trntensor_b200.inputs import ao2mo_inputs
+
+    lib = _lib.load()
+    dev = torch.device("cuda", local)
+    c = AO_CONFIG
+    nbf, nocc, nvir, naux = c["nbf"], c["nocc"], c["nvir"], c["naux"]
+    eri, co, cv = ao2mo_inputs(nbf, nocc, nvir, naux, seed=0, device=dev)
+    p0, p1 = distributed.aux_slab(naux, rank, world)
+    slab = eri[:, :, p0:p1].contiguous()
+    nl = p1 - p0
+    del eri
+    out = torch.empty(nocc, nvir, nl, dtype=torch.float32, device=dev)
+    ws_bytes = int(lib.tt_ao2mo_workspace_bytes(nbf, nocc, nvir, nl, 4))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        _lib.check(lib.tt_ao2mo_f32(P(slab), P(co), P(cv), nbf, nocc, nvir, nl, P(ws), ws_bytes,
+                                    P(out), sp), "tt_ao2mo_f32")
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world, dev)
+    alg_bytes = 4.0 * (nbf * nbf * naux + nbf * (nocc + nvir) * world + nocc * nvir * naux)
+    flops = 2.0 * nocc * nbf * nbf * naux + 2.0 * nocc * nvir * nbf * naux
+    res = {"workload": "ao2mo_config3", **c, "ms": ms, "GB_per_s": alg_bytes / ms / 1e6,
+           "TFLOP_per_s": flops / ms / 1e9, "algorithmic_bytes": alg_bytes, "flops": flops,
+           "parallelism": f"aux index split over {world} GPU(s), no communication",
+           "kernels": "CUDA-core two-step GEMM (fp32)"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import numpy as np
+
+        from oracle import oracle
+
+        w = 16
+        e_np = slab[:, :, :w].cpu().numpy()
+        co_np, cv_np = co.cpu().numpy(), cv.cpu().numpy()
+        oracle.ao_to_mo_two_step(e_np, co_np, cv_np)
+        t0 = time.perf_counter()
+        oracle.ao_to_mo_two_step(e_np, co_np, cv_np)
+        t_cpu = (time.perf_counter() - t0) * naux / w
+        res["cpu_baseline"] = {"ms": t_cpu * 1e3, "cores": _blas_threads(), "kind": "port",
+                               "sample": f"two-step einsum port on a {w}-wide aux slab (fp32), "
+                                         f"extrapolated x{naux // w}"}
+    del slab, ws, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args, rank, world, local):
     import trntensor_b200 as tt
     from trntensor_b200 import _lib, distributed
@@ -425,8 +494,9 @@ def run_ours(args, rank, world, local):
     e2e = None
     if not args.no_e2e:
         Bh = B.cpu().pin_memory()
+        q = None  # slices no longer needed; the API allocates its own workspace
+        torch.cuda.empty_cache()
         eoh, evh = eo.cpu(), ev.cpu()
-        del q
         api = tt.mp2_energy if world == 1 else distributed.mp2_energy
         api(Bh, eoh, evh)  # warm-up (allocator, workspace)
         torch.cuda.synchronize(dev)
@@ -458,6 +528,12 @@ def run_ours(args, rank, world, local):
                          f"{nocc}^2 ordered pairs = {t_job:.0f} s",
                "host_cpus": os.cpu_count()}
 
+    ao = None
+    if not args.no_ao2mo:
+        del B, q, sc
+        torch.cuda.empty_cache()
+        ao = measure_ao2mo(args, rank, world, local)
+
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -485,6 +561,7 @@ def run_ours(args, rank, world, local):
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,
             "clocks": clk,
+            "ao2mo": ao,
         }
         print(json.dumps(line), flush=True)
 
