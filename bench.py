@@ -365,7 +365,7 @@ def measure_ao2mo(args, rank, world, local):
     res = {"workload": "ao2mo_config3", **c, "ms": ms, "GB_per_s": alg_bytes / ms / 1e6,
            "TFLOP_per_s": flops / ms / 1e9, "algorithmic_bytes": alg_bytes, "flops": flops,
            "parallelism": f"aux index split over {world} GPU(s), no communication",
-           "kernels": "CUDA-core two-step GEMM (fp32)"}
+           "kernels": "int8 Ozaki tcgen05 GEMMs (column-scaled slices), two steps"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
 

@@ -136,24 +136,34 @@ int tt_mp2_energy_simt_f32(const float* B, const float* eps_occ, const float* ep
 
 /* ------------------------------------------------------------ AO -> MO */
 
-/* Workspace bytes of the (nocc, nbf, naux) intermediate for tt_ao2mo_f32
- * (elem_bytes 4) or tt_ao2mo_f64 (elem_bytes 8). */
+/* Workspace bytes for tt_ao2mo_f32 (elem_bytes 4: int8 slices of every
+ * operand, the fp32 intermediate and its slices) or tt_ao2mo_f64 /
+ * tt_ao2mo_simt_f32 (elem_bytes 8 / 4 are enough: the (nocc, nbf, naux)
+ * intermediate). */
 size_t tt_ao2mo_workspace_bytes(int nbf, int nocc, int nvir, int naux, int elem_bytes);
 
 /*
- * B[i,a,P] = sum_{m,n} C_occ[m,i] C_vir[n,a] eri[m,n,P], in two steps with
- * the (i, n, P) intermediate in the caller's workspace:
+ * B[i,a,P] = sum_{m,n} C_occ[m,i] C_vir[n,a] eri[m,n,P] on int8 tensor cores
+ * (Ozaki splitting with per-column scales along each contraction index; six
+ * exact int32-accumulated slice GEMMs per step), in two steps with the
+ * (i, n, P) intermediate in the caller's workspace:
  *   inter = einsum("mi,mnP->inP"), B = einsum("na,inP->iaP").
  * eri (nbf, nbf, naux), C_occ (nbf, nocc), C_vir (nbf, nvir), B_out
  * (nocc, nvir, naux), all contiguous row-major. For a P-sharded run pass the
- * rank's contiguous (nbf, nbf, naux_local) slab.
+ * rank's contiguous (nbf, nbf, naux_local) slab. dev_status (device int) is
+ * zeroed and receives a nonzero code if a device wait ran out.
  * Replaces trntensor/nki/dispatch.py:286-336 (_nki_ao_to_mo_transform) and
  * trntensor/nki/_kernels.py:209-296 (ao_to_mo_transform_kernel); the math is
  * trntensor/quantum.py:188-194.
  */
 int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf, int nocc,
                  int nvir, int naux, void* workspace, size_t workspace_bytes, float* B_out,
-                 void* stream);
+                 int* dev_status, void* stream);
+
+/* Diagnostic: the same transform in plain fp32 on CUDA cores. */
+int tt_ao2mo_simt_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf,
+                      int nocc, int nvir, int naux, void* workspace, size_t workspace_bytes,
+                      float* B_out, void* stream);
 
 /* The same in fp64 (precision="kahan" and float64 inputs). */
 int tt_ao2mo_f64(const double* eri, const double* C_occ, const double* C_vir, int nbf,

@@ -90,3 +90,19 @@ def test_config3_p_slab(cuda_ok):
         assert max_rel(B[:, :, p0:p0 + 16].cpu().numpy(), ref) <= TOL_F32
         B64 = tt.ao_to_mo_transform(eri[:, :, p0:p0 + 16].double(), co.double(), cv.double())
         assert max_rel(B64.cpu().numpy(), ref) <= TOL_F64
+
+
+@pytest.mark.parametrize("shape", [(200, 10, 20, 24), (128, 16, 112, 384), (300, 130, 70, 50)])
+def test_tensor_core_vs_cuda_core(cuda_ok, shape):
+    """The int8-Ozaki tensor-core path and the plain fp32 CUDA-core path agree
+    with the fp64 path (ragged tiles in every dimension)."""
+    from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
+
+    nbf, nocc, nvir, naux = shape
+    eri, co, cv = ao2mo_inputs(nbf, nocc, nvir, naux, seed=4) if nbf >= nocc + nvir else (
+        torch.randn(nbf, nbf, naux) * 0.1, torch.randn(nbf, nocc), torch.randn(nbf, nvir))
+    ref = _cuda_ao_to_mo_transform(eri.double(), co.double(), cv.double()).cpu().numpy()
+    tc = _cuda_ao_to_mo_transform(eri, co, cv, kernel="tc").cpu().numpy()
+    simt = _cuda_ao_to_mo_transform(eri, co, cv, kernel="simt").cpu().numpy()
+    assert max_rel(tc, ref) <= TOL_F32
+    assert max_rel(simt, ref) <= TOL_F32

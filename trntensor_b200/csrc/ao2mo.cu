@@ -1,6 +1,7 @@
 // C-ABI entry points for the AO->MO transform (two-step form).
 #include "ao2mo_simt.cuh"
 #include "common.cuh"
+#include "ozaki_gemm.cuh"
 
 namespace tt {
 namespace {
@@ -13,8 +14,79 @@ int setup(int dev) {
   return once_per_device(g_flags, g_ok, dev, [dev]() -> int {
     if (cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return TT_ERR_CUDA;
+    if (cudaFuncSetAttribute(oz::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             oz::kSmemBytes) != cudaSuccess)
+      return TT_ERR_CUDA;
     return TT_OK;
   });
+}
+
+inline size_t pad16(size_t x) { return (x + 15) / 16 * 16; }
+inline size_t al256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Layout of the tensor-core workspace (all offsets 256-byte aligned).
+struct OzLayout {
+  size_t qo, so, qv, sv, qe, se, inter, qi, si, total;
+  OzLayout(size_t nbf, size_t nocc, size_t nvir, size_t naux) {
+    size_t o = 0;
+    auto take = [&o](size_t bytes) { size_t r = o; o += al256(bytes); return r; };
+    qo = take(3 * nbf * pad16(nocc));
+    so = take(4 * pad16(nocc));
+    qv = take(3 * nbf * pad16(nvir));
+    sv = take(4 * pad16(nvir));
+    qe = take(3 * nbf * pad16(nbf * naux));
+    se = take(4 * pad16(nbf * naux));
+    inter = take(4 * nocc * nbf * naux);
+    qi = take(3 * nocc * nbf * pad16(naux));
+    si = take(4 * nocc * pad16(naux));
+    total = o;
+  }
+};
+
+int split_cols(const float* X, long long ldx, long long bsx, int batch, int K, int N, int npad,
+               int8_t* Q, float* S, cudaStream_t s, int sms) {
+  const long long nblk = (long long)batch * ((npad + oz::kSplitCols - 1) / oz::kSplitCols);
+  const long long cap = (long long)sms * 8;
+  const int grid = (int)(nblk < cap ? nblk : cap);
+  oz::colmax_kernel<<<grid, oz::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S);
+  oz::slice_kernel<<<grid, oz::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S, Q);
+  return cuda_status(cudaGetLastError());
+}
+
+// Tensor map over slice planes Q[3][batch][K][npad] (bytes), box 128 x 64 x 1 x 3.
+int slice_map(CUtensorMap* m, const int8_t* Q, int npad, int K, int batch) {
+  const uint64_t dims[4] = {(uint64_t)npad, (uint64_t)K, (uint64_t)batch, 3};
+  const uint64_t strides[3] = {(uint64_t)npad, (uint64_t)npad * K, (uint64_t)npad * K * batch};
+  const uint32_t box[4] = {(uint32_t)oz::kTile, (uint32_t)oz::kKC, 1, 3};
+  return encode_tmap(m, Q, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_DATA_TYPE_UINT8);
+}
+
+int oz_gemm(const int8_t* QA, const float* SA, int mpad, int batchA, const int8_t* QB,
+            const float* SB, int npad, int batch, int M, int N, int K, float* C, long long ldc,
+            long long strideC, int* err, cudaStream_t s, int sms) {
+  CUtensorMap ma, mb;
+  if (slice_map(&ma, QA, mpad, K, batchA) || slice_map(&mb, QB, npad, K, batch)) return TT_ERR_TMA;
+  oz::Params p;
+  p.sA = SA;
+  p.sB = SB;
+  p.ldsA = mpad;
+  p.ldsB = npad;
+  p.C = C;
+  p.ldc = ldc;
+  p.strideC = strideC;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.batch = batch;
+  p.shared_A = batchA == 1 && batch > 1;
+  p.tiles_m = (M + oz::kTile - 1) / oz::kTile;
+  p.tiles_n = (N + oz::kTile - 1) / oz::kTile;
+  p.err = err;
+  const long long tiles = (long long)p.tiles_m * p.tiles_n * batch;
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  oz::gemm_kernel<<<grid, oz::kThreads, oz::kSmemBytes, s>>>(ma, mb, p);
+  return cuda_status(cudaGetLastError());
 }
 
 template <typename T>
@@ -66,11 +138,59 @@ extern "C" {
 
 size_t tt_ao2mo_workspace_bytes(int nbf, int nocc, int nvir, int naux, int elem_bytes) {
   if (nbf <= 0 || nocc <= 0 || nvir <= 0 || naux <= 0) return 0;
-  if (elem_bytes != 4 && elem_bytes != 8) return 0;
-  return (size_t)nocc * nbf * naux * (size_t)elem_bytes;
+  if (elem_bytes == 4) return tt::OzLayout(nbf, nocc, nvir, naux).total;
+  if (elem_bytes == 8) return (size_t)nocc * nbf * naux * 8;
+  return 0;
 }
 
 int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf, int nocc,
+                 int nvir, int naux, void* workspace, size_t workspace_bytes, float* B_out,
+                 int* dev_status, void* stream) {
+  using namespace tt;
+  if (!eri || !C_occ || !C_vir || !workspace || !B_out || !dev_status) return TT_ERR_NULL;
+  if (nbf <= 0 || nocc <= 0 || nvir <= 0 || naux <= 0) return TT_ERR_SHAPE;
+  if ((long long)nbf * naux > 0x7fffffffLL) return TT_ERR_SHAPE;
+  const OzLayout L(nbf, nocc, nvir, naux);
+  if (workspace_bytes < L.total) return TT_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return TT_ERR_ALIGN;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = setup(dev);
+  if (st != TT_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  TT_CUDA(cudaMemsetAsync(dev_status, 0, sizeof(int), s));
+  char* w = static_cast<char*>(workspace);
+  int8_t* qo = (int8_t*)(w + L.qo);
+  float* so = (float*)(w + L.so);
+  int8_t* qv = (int8_t*)(w + L.qv);
+  float* sv = (float*)(w + L.sv);
+  int8_t* qe = (int8_t*)(w + L.qe);
+  float* se = (float*)(w + L.se);
+  float* inter = (float*)(w + L.inter);
+  int8_t* qi = (int8_t*)(w + L.qi);
+  float* si = (float*)(w + L.si);
+  const int sms = g_sms[dev];
+  const int po = (int)pad16(nocc), pv = (int)pad16(nvir), pe = (int)pad16((size_t)nbf * naux),
+            pa = (int)pad16(naux);
+  // Column-scaled int8 slices of the three operands of step 1 and of C_vir.
+  if ((st = split_cols(C_occ, nocc, 0, 1, nbf, nocc, po, qo, so, s, sms))) return st;
+  if ((st = split_cols(C_vir, nvir, 0, 1, nbf, nvir, pv, qv, sv, s, sms))) return st;
+  if ((st = split_cols(eri, (long long)nbf * naux, 0, 1, nbf, nbf * naux, pe, qe, se, s, sms)))
+    return st;
+  // step 1: inter[i][(n,P)] = sum_m C_occ[m][i] eri[m][(n,P)]
+  if ((st = oz_gemm(qo, so, po, 1, qe, se, pe, 1, nocc, nbf * naux, nbf, inter,
+                    (long long)nbf * naux, 0, dev_status, s, sms)))
+    return st;
+  // slices of inter[i] (K = n, N = P), scales per (i, P)
+  if ((st = split_cols(inter, naux, (long long)nbf * naux, nocc, nbf, naux, pa, qi, si, s, sms)))
+    return st;
+  // step 2: B_out[i][a][P] = sum_n C_vir[n][a] inter[i][n][P]
+  return oz_gemm(qv, sv, pv, 1, qi, si, pa, nocc, nvir, naux, nbf, B_out, naux,
+                 (long long)nvir * naux, dev_status, s, sms);
+}
+
+int tt_ao2mo_simt_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf, int nocc,
                  int nvir, int naux, void* workspace, size_t workspace_bytes, float* B_out,
                  void* stream) {
   return tt::ao2mo_simt<float>(eri, C_occ, C_vir, nbf, nocc, nvir, naux, workspace,

@@ -1,0 +1,340 @@
+// fp32 GEMM on int8 tensor cores by Ozaki splitting, for operands stored
+// "K rows, M/N contiguous" (MN-major), batched:
+//   C[b][m][n] = sum_k A[bA][k][m] B[b][k][n]
+// Each operand column (fixed m or n, all k) gets a power-of-two scale s and
+// three int8 slices: X[k][c] = s_c (q1 + q2/2^7 + q3/2^14)[k][c] + O(2^-22).
+// Then C = sA_m sB_n (L2 + L3/2^7 + L4/2^14) with six exact int8 GEMMs
+// accumulated in int32 TMEM (see csrc/mp2_i8.cuh for the same scheme on
+// K-major rows). Used for both steps of the AO->MO transform.
+//
+// Tile: M = N = 128 (one 128-byte SW128 atom wide in M/N), 64 k per stage.
+// Roles: warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue.
+#pragma once
+#include "ptx.cuh"
+
+namespace tt {
+namespace oz {
+
+constexpr int kTile = 128;
+constexpr int kKC = 64;
+constexpr int kStages = 3;
+constexpr int kSliceTile = kTile * kKC;          // 8 KB
+constexpr int kOperandBytes = 3 * kSliceTile;    // 24 KB
+constexpr int kStageBytes = 2 * kOperandBytes;   // 48 KB
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageLd = kTile + 4;  // padded fp32 row of the output staging tile
+constexpr int kOutStageBytes = kTile * kStageLd * 4;
+constexpr int kSmemBytes = kStages * kStageBytes + kOutStageBytes + 1024 + 256;
+
+struct Params {
+  const float* sA;  // [batchA][ldsA] column scales of A
+  const float* sB;  // [batch][ldsB]
+  long long ldsA, ldsB;
+  float* C;
+  long long ldc, strideC;
+  int M, N, K, batch;
+  int shared_A;     // 1: every batch uses A batch 0
+  int tiles_m, tiles_n;
+  int* err;
+};
+
+__device__ __forceinline__ float level_combine(int l2, int l3, int l4) {
+  return (float)l2 + (float)l3 * (1.0f / 128.0f) + (float)l4 * (1.0f / 16384.0f);
+}
+
+struct Tile {
+  int b, m0, n0;
+};
+__device__ inline Tile tile_decode(long long w, const Params& p) {
+  // batch-major, then n tile, then m tile: consecutive tiles share B
+  Tile t;
+  const long long per_b = (long long)p.tiles_m * p.tiles_n;
+  t.b = (int)(w / per_b);
+  const int r = (int)(w % per_b);
+  t.n0 = (r / p.tiles_m) * kTile;
+  t.m0 = (r % p.tiles_m) * kTile;
+  return t;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  float* ostage = (float*)(smem + kStages * kStageBytes);
+  uint64_t* full = (uint64_t*)(smem + kStages * kStageBytes + kOutStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* final_bar = acc_empty + 1;
+  uint32_t* tmem_slot = (uint32_t*)(final_bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long n_tiles = (long long)p.tiles_m * p.tiles_n * p.batch;
+  const int nkc = (p.K + kKC - 1) / kKC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 32 * kEpiWarps);
+    mbar_init(final_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&mapA);
+    tma_prefetch_desc(&mapB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
+        const Tile t = tile_decode(w, p);
+        const int bA = p.shared_A ? 0 : t.b;
+        for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          tma_load_4d(st, &mapA, &full[s], t.m0, kc * kKC, bA, 0);
+          tma_load_4d(st + kOperandBytes, &mapB, &full[s], t.n0, kc * kKC, t.b, 0);
+        }
+      }
+      const uint32_t issued = it;
+      for (uint32_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k)
+        mbar_wait_drain(&full[k % kStages], (k / kStages) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8(kTile, kTile, 1, 1);
+      uint32_t it = 0, round = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x, ++round) {
+        if (!mbar_wait(acc_empty, (round & 1u) ^ 1u, p.err, kDevTimeoutAccFree)) break;
+        tc_fence_after();
+        for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&full[s], (it / kStages) & 1u, p.err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + kOperandBytes;
+#pragma unroll
+          for (int ks = 0; ks < kKC / 32; ++ks) {
+            // MN-major SW128: 8 k-rows of 128 B per 1 KB atom; 32 k = 4 atoms.
+            uint64_t a[3], b[3];
+#pragma unroll
+            for (int t = 0; t < 3; ++t) {
+              a[t] = smem_desc(sa + t * kSliceTile + ks * 4096, 8192, 1024, 2);
+              b[t] = smem_desc(sb + t * kSliceTile + ks * 4096, 8192, 1024, 2);
+            }
+            const uint32_t first = (kc | ks) != 0;
+            mma_i8_fill(tmem + 0 * kTile, a[0], b[0], idesc, first);
+            mma_i8_use(tmem + 1 * kTile, a[0], b[1], idesc, first);
+            mma_i8_lastuse(tmem + 2 * kTile, a[0], b[2], idesc, first);
+            mma_i8_fill(tmem + 1 * kTile, a[1], b[0], idesc, 1);
+            mma_i8_lastuse(tmem + 2 * kTile, a[1], b[1], idesc, 1);
+            mma_i8(tmem + 2 * kTile, a[2], b[0], idesc, 1);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(acc_full);
+      }
+      mma_commit(final_bar);
+      mbar_wait_drain(final_bar, 0);
+    }
+  } else {
+    // Drain TMEM into a padded shared-memory tile, free TMEM for the next
+    // tile's MMAs, then write the tile with coalesced row segments.
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int c0 = (ew >> 2) * (kTile / 2);
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                     (p.strideC % 4 == 0);
+    uint32_t round = 0;
+    for (long long w = blockIdx.x; w < n_tiles; w += gridDim.x, ++round) {
+      if (!mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)) break;
+      tc_fence_after();
+      const Tile t = tile_decode(w, p);
+      const int bA = p.shared_A ? 0 : t.b;
+      const int m = t.m0 + row;
+      const float sa = m < p.M ? __ldg(p.sA + bA * p.ldsA + m) : 0.f;
+      const float* sbp = p.sB + t.b * p.ldsB;
+      // the previous tile's stores must be done reading the staging tile
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps));
+      for (int c = c0; c < c0 + kTile / 2; c += 16) {
+        int l2[16], l3[16], l4[16];
+        tmem_ld16i(lane_base + 0 * kTile + c, l2);
+        tmem_ld16i(lane_base + 1 * kTile + c, l3);
+        tmem_ld16i(lane_base + 2 * kTile + c, l4);
+        tmem_ld_wait();
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int n = t.n0 + c + k;
+          const float sb = n < p.N ? __ldg(sbp + n) : 0.f;
+          v[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
+        }
+        float4* dst = reinterpret_cast<float4*>(ostage + row * kStageLd + c);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps));
+      float* Cb = p.C + t.b * p.strideC;
+      const int nn = p.N - t.n0 < kTile ? p.N - t.n0 : kTile;
+      for (int r = ew; r < kTile; r += kEpiWarps) {
+        const int mm = t.m0 + r;
+        if (mm >= p.M) break;
+        float* crow = Cb + (long long)mm * p.ldc + t.n0;
+        const float* srow = ostage + r * kStageLd;
+        if (vec && nn == kTile) {
+          reinterpret_cast<float4*>(crow)[lane] = reinterpret_cast<const float4*>(srow)[lane];
+        } else {
+          for (int c = lane; c < nn; c += 32) crow[c] = srow[c];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Column-scaled Ozaki split of X[b][k][n] (row stride ldx, batch stride bsx):
+// S[b][n] = 2^(e-7) with max_k |X[b][k][n]| 2^(7-e) <= 127; Q[t][b][k][n]
+// (row length npad, zero padding) the three int8 slices. One block handles 32
+// columns of one batch for all k.
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
+
+// Column-scaled split in two streaming passes over X[b][k][n]:
+//   colmax_kernel: S[b][n] = power-of-two scale of column n (max over k);
+//   slice_kernel : Q[t][b][k][n] int8 slices with that scale.
+// A block covers 128 columns (4 per lane, 16-byte accesses when the row
+// stride allows) and all k; its 8 warps take every 8th row.
+constexpr int kSplitThreads = 256;
+constexpr int kSplitCols = 128;
+
+__device__ __forceinline__ float scale_for_max(float mx) {
+  if (!(mx > 1.0e-30f && mx < 3.0e38f)) return 0.f;
+  int e = ilogbf(mx) + 1;
+  if (mx * pow2f(7 - e) > 127.f) ++e;
+  return pow2f(e - 7);
+}
+
+__device__ __forceinline__ void load4(const float* xc, bool vec, int nvalid, float (&v)[4]) {
+  if (vec && nvalid >= 4) {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(xc));
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = j < nvalid ? __ldg(xc + j) : 0.f;
+  }
+}
+
+__global__ void __launch_bounds__(kSplitThreads)
+    colmax_kernel(const float* __restrict__ X, long long ldx, long long bsx, int batch, int K,
+                  int N, int npad, float* __restrict__ S) {
+  __shared__ float red[kSplitThreads / 32][kSplitCols];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int ncb = (npad + kSplitCols - 1) / kSplitCols;
+  const bool vec = (ldx % 4 == 0) && (bsx % 4 == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
+  for (long long blk = blockIdx.x; blk < (long long)batch * ncb; blk += gridDim.x) {
+    const int b = (int)(blk / ncb);
+    const int n = (int)(blk % ncb) * kSplitCols + lane * 4;
+    const int nvalid = N - n;
+    const float* xc = X + b * bsx + n;
+    float mx[4] = {0.f, 0.f, 0.f, 0.f};
+    if (nvalid > 0) {
+#pragma unroll 4
+      for (int k = wp; k < K; k += kSplitThreads / 32) {
+        float v[4];
+        load4(xc + (long long)k * ldx, vec, nvalid, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mx[j] = fmaxf(mx[j], fabsf(v[j]));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[wp][lane * 4 + j] = mx[j];
+    __syncthreads();
+    if (threadIdx.x < kSplitCols) {
+      float m = 0.f;
+#pragma unroll
+      for (int w = 0; w < kSplitThreads / 32; ++w) m = fmaxf(m, red[w][threadIdx.x]);
+      const int nn = (int)(blk % ncb) * kSplitCols + threadIdx.x;
+      if (nn < npad) S[(long long)b * npad + nn] = nn < N ? scale_for_max(m) : 0.f;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kSplitThreads)
+    slice_kernel(const float* __restrict__ X, long long ldx, long long bsx, int batch, int K, int N,
+                 int npad, const float* __restrict__ S, int8_t* __restrict__ Q) {
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int ncb = (npad + kSplitCols - 1) / kSplitCols;
+  const long long plane = (long long)batch * K * npad;
+  const bool vec = (ldx % 4 == 0) && (bsx % 4 == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
+  for (long long blk = blockIdx.x; blk < (long long)batch * ncb; blk += gridDim.x) {
+    const int b = (int)(blk / ncb);
+    const int n = (int)(blk % ncb) * kSplitCols + lane * 4;
+    if (n >= npad) continue;
+    const int nvalid = N - n;
+    const float* xc = X + b * bsx + n;
+    float inv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float sc = S[(long long)b * npad + n + j];
+      inv[j] = sc > 0.f ? 1.0f / sc : 0.f;  // exact: sc is a power of two
+    }
+    int8_t* q1 = Q + (long long)b * K * npad + n;
+#pragma unroll 4
+    for (int k = wp; k < K; k += kSplitThreads / 32) {
+      float v[4];
+      if (nvalid > 0) load4(xc + (long long)k * ldx, vec, nvalid, v);
+      else v[0] = v[1] = v[2] = v[3] = 0.f;
+      uint32_t w1 = 0, w2 = 0, w3 = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x = v[j] * inv[j];
+        const float d1 = rintf(x);
+        const float r1 = (x - d1) * 128.f;
+        const float d2 = rintf(r1);
+        const float d3 = rintf((r1 - d2) * 128.f);
+        w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * j);
+        w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * j);
+        w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * j);
+      }
+      const long long o = (long long)k * npad;
+      *reinterpret_cast<uint32_t*>(q1 + o) = w1;
+      *reinterpret_cast<uint32_t*>(q1 + o + plane) = w2;
+      *reinterpret_cast<uint32_t*>(q1 + o + 2 * plane) = w3;
+    }
+  }
+}
+
+}  // namespace oz
+}  // namespace tt

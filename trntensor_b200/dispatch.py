@@ -187,8 +187,12 @@ def _cuda_ao_to_mo_transform(
     C_vir: torch.Tensor,
     *,
     precision: str = "fast",
+    kernel: str = "tc",
 ) -> torch.Tensor:
     """AO->MO transform on the current CUDA device; result stays on the device.
+
+    ``kernel="tc"``: int8 Ozaki tensor cores (fp32 product path);
+    ``kernel="simt"``: plain fp32 CUDA-core cross-check.
 
     fp32 inputs compute in fp32, float64 inputs or ``precision="kahan"`` in
     fp64 (trntensor/einsum.py:108-111 semantics: the caller casts back).
@@ -207,8 +211,16 @@ def _cuda_ao_to_mo_transform(
     esz = 8 if cdt == torch.float64 else 4
     ws_bytes = int(lib.tt_ao2mo_workspace_bytes(nbf, nocc, nvir, naux, esz))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    fn = lib.tt_ao2mo_f64 if cdt == torch.float64 else lib.tt_ao2mo_f32
-    st = fn(_ptr(e), _ptr(co), _ptr(cv), nbf, nocc, nvir, naux, _ptr(ws), ws_bytes, _ptr(out),
-            ctypes.c_void_p(_stream_handle()))
-    _lib.check(st, "tt_ao2mo")
+    stream = ctypes.c_void_p(_stream_handle())
+    if cdt == torch.float64 or kernel == "simt":
+        fn = lib.tt_ao2mo_f64 if cdt == torch.float64 else lib.tt_ao2mo_simt_f32
+        st = fn(_ptr(e), _ptr(co), _ptr(cv), nbf, nocc, nvir, naux, _ptr(ws), ws_bytes,
+                _ptr(out), stream)
+        _lib.check(st, "tt_ao2mo")
+        return out
+    dev_status = torch.empty((), dtype=torch.int32, device=dev)
+    st = lib.tt_ao2mo_f32(_ptr(e), _ptr(co), _ptr(cv), nbf, nocc, nvir, naux, _ptr(ws), ws_bytes,
+                          _ptr(out), _ptr(dev_status), stream)
+    _lib.check(st, "tt_ao2mo_f32")
+    _check_status(dev_status, "tt_ao2mo_f32")
     return out
