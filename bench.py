@@ -342,12 +342,13 @@ def measure_ao2mo(args, rank, world, local):
     out = torch.empty(nocc, nvir, nl, dtype=torch.float32, device=dev)
     ws_bytes = int(lib.tt_ao2mo_workspace_bytes(nbf, nocc, nvir, nl, 4))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    status = torch.zeros((), dtype=torch.int32, device=dev)
     sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
     def step():
         _lib.check(lib.tt_ao2mo_f32(P(slab), P(co), P(cv), nbf, nocc, nvir, nl, P(ws), ws_bytes,
-                                    P(out), sp), "tt_ao2mo_f32")
+                                    P(out), P(status), sp), "tt_ao2mo_f32")
 
     for _ in range(args.warmup):
         step()
@@ -360,6 +361,8 @@ def measure_ao2mo(args, rank, world, local):
     b.record()
     torch.cuda.synchronize(dev)
     ms = max_over_ranks(a.elapsed_time(b) / args.steps, world, dev)
+    if int(status.item()) != 0:
+        raise RuntimeError(f"AO->MO device status 0x{int(status.item()):x}")
     alg_bytes = 4.0 * (nbf * nbf * naux + nbf * (nocc + nvir) * world + nocc * nvir * naux)
     flops = 2.0 * nocc * nbf * nbf * naux + 2.0 * nocc * nvir * nbf * naux
     res = {"workload": "ao2mo_config3", **c, "ms": ms, "GB_per_s": alg_bytes / ms / 1e6,
@@ -532,7 +535,10 @@ def run_ours(args, rank, world, local):
     if not args.no_ao2mo:
         del B, q, sc
         torch.cuda.empty_cache()
-        ao = measure_ao2mo(args, rank, world, local)
+        try:
+            ao = measure_ao2mo(args, rank, world, local)
+        except Exception as exc:  # keep the headline line; report the failure
+            ao = {"error": f"{type(exc).__name__}: {exc}"}
 
     if rank == 0:
         line = {
