@@ -44,7 +44,11 @@ constexpr int kOperandBytes = kSlices * kSliceTile;  // 24 KB
 constexpr int kStageBytes = 2 * kOperandBytes;       // A and B: 48 KB
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+// Diagonal blocks (A == B) of an i != j pair need y = x^T: x is exchanged
+// through a padded shared-memory half-tile (64 rows x 129 floats) in two rounds.
+constexpr int kTLd = kBlk + 1;
+constexpr int kTBytes = (kBlk / 2) * kTLd * 4;
+constexpr int kSmemBytes = kStages * kStageBytes + kTBytes + 1024 + 256;
 constexpr int kColStash = 3 * kBlk;       // TMEM column of the parked x
 
 struct Params {
@@ -76,6 +80,9 @@ __device__ inline void pair_decode(long long p, int n, int& i, int& j) {
 
 struct Item {
   int i, j, a0, b0;
+  // One accumulation phase is enough when y follows from x: i == j gives
+  // T symmetric (y = x), a diagonal block gives y = x^T.
+  __device__ bool single() const { return i == j || a0 == b0; }
 };
 __device__ inline Item item_decode(long long w, const Params& p) {
   const int nbp = p.nblk * (p.nblk + 1) / 2;
@@ -99,7 +106,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     energy_kernel(const __grid_constant__ CUtensorMap mapQ, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(smem + kStages * kStageBytes);
+  float* tbuf = (float*)(smem + kStages * kStageBytes);
+  uint64_t* full = (uint64_t*)(smem + kStages * kStageBytes + kTBytes);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 1;
@@ -139,7 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (long long w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
         const Item t = item_decode(w, p);
-        for (int ph = 0; ph < 2 && ok; ++ph) {
+        const int nph = t.single() ? 1 : 2;
+        for (int ph = 0; ph < nph && ok; ++ph) {
           const int occA = ph == 0 ? t.i : t.j;
           const int occB = ph == 0 ? t.j : t.i;
           for (int kc = 0; kc < nkc; ++kc, ++it) {
@@ -170,7 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
       bool ok = true;
       for (long long w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
-        for (int ph = 0; ph < 2 && ok; ++ph, ++round) {
+        const int nph = item_decode(w, p).single() ? 1 : 2;
+        for (int ph = 0; ph < nph && ok; ++ph, ++round) {
 #ifdef TT_MP2_PROFILE
           long long t0 = clock64();
 #endif
@@ -252,7 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int a = t.a0 + row;
       const bool arow = a < p.nvir;
       // ---- phase x: park s_ia s_jb (L2 + L3/2^7 + L4/2^14) in the stash columns
-      if (!mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)) break;
+      if (!group_all<32 * kEpiWarps>(mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)))
+        break;
       tc_fence_after();
       {
         const float sa = arow ? __ldg(p.scale + (long long)t.i * p.nvir + a) : 0.f;
@@ -276,43 +287,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(acc_empty);
       ++round;
-      // ---- phase y: combine with the parked x and reduce the energy
-      if (!mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)) break;
-      tc_fence_after();
       double acc = 0.0;
-      {
+      const float eija = arow ? (__ldg(p.eps_occ + t.i) + __ldg(p.eps_occ + t.j)) -
+                                    __ldg(p.eps_vir + a)
+                              : 0.f;
+      // sum over this thread's 16 columns starting at c of the (a,b)+(b,a) terms
+      auto chunk_energy = [&](int c, const float (&x)[16], const float (&y)[16]) {
+        float part = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int b = t.b0 + c + k;
+          if (arow && b < p.nvir && a <= b) {
+            const float den = eija - __ldg(p.eps_vir + b);
+            float v = 2.f * (x[k] * x[k] - x[k] * y[k] + y[k] * y[k]) / den;
+            if (a == b) v *= 0.5f;
+            part += v;
+          }
+        }
+        return (double)part;
+      };
+      if (t.i == t.j) {
+        // ---- T_ii is symmetric: y = x
+        for (int c = c0; c < c0 + kBlk / 2; c += 16) {
+          float x[16];
+          tmem_ld16(lane_base + kColStash + c, x);
+          tmem_ld_wait();
+          acc += chunk_energy(c, x, x);
+        }
+      } else if (t.a0 == t.b0) {
+        // ---- diagonal block: y[a][b] = x[b][a], exchanged through shared memory.
+        // Round r: the warps holding rows [64r, 64r+64) publish them; the warps
+        // whose columns are [64r, 64r+64) read their transposed values.
+        for (int r = 0; r < 2; ++r) {
+          asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps));
+          if ((q >> 1) == r) {
+            for (int c = c0; c < c0 + kBlk / 2; c += 16) {
+              float x[16];
+              tmem_ld16(lane_base + kColStash + c, x);
+              tmem_ld_wait();
+#pragma unroll
+              for (int k = 0; k < 16; ++k) tbuf[(row - 64 * r) * kTLd + c + k] = x[k];
+            }
+          }
+          asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps));
+          if ((c0 >> 6) == r) {
+            for (int c = c0; c < c0 + kBlk / 2; c += 16) {
+              float x[16], y[16];
+              tmem_ld16(lane_base + kColStash + c, x);
+              tmem_ld_wait();
+#pragma unroll
+              for (int k = 0; k < 16; ++k) y[k] = tbuf[(c + k - 64 * r) * kTLd + row];
+              acc += chunk_energy(c, x, y);
+            }
+          }
+        }
+      } else {
+        // ---- phase y: combine with the parked x and reduce the energy
+        if (!group_all<32 * kEpiWarps>(mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)))
+          break;
+        tc_fence_after();
         const float sa = arow ? __ldg(p.scale + (long long)t.j * p.nvir + a) : 0.f;
-        const float eija = arow ? (__ldg(p.eps_occ + t.i) + __ldg(p.eps_occ + t.j)) -
-                                      __ldg(p.eps_vir + a)
-                                : 0.f;
         for (int c = c0; c < c0 + kBlk / 2; c += 16) {
           int l2[16], l3[16], l4[16];
-          float x[16];
+          float x[16], y[16];
           tmem_ld16i(lane_base + 0 * kBlk + c, l2);
           tmem_ld16i(lane_base + 1 * kBlk + c, l3);
           tmem_ld16i(lane_base + 2 * kBlk + c, l4);
           tmem_ld16(lane_base + kColStash + c, x);
           tmem_ld_wait();
-          float part = 0.f;
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
             const int b = t.b0 + c + k;
-            if (arow && b < p.nvir && a <= b) {
-              const float sb = __ldg(p.scale + (long long)t.i * p.nvir + b);
-              const float y = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
-              const float xv = x[k];
-              const float den = eija - __ldg(p.eps_vir + b);
-              float v = 2.f * (xv * xv - xv * y + y * y) / den;
-              if (a == b) v *= 0.5f;
-              part += v;
-            }
+            const float sb = b < p.nvir ? __ldg(p.scale + (long long)t.i * p.nvir + b) : 0.f;
+            y[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
           }
-          acc += (double)part;
+          acc += chunk_energy(c, x, y);
         }
+        tc_fence_before();
+        mbar_arrive(acc_empty);
+        ++round;
       }
-      tc_fence_before();
-      mbar_arrive(acc_empty);
-      ++round;
       const double wgt = (t.i == t.j) ? 1.0 : 2.0;
       my_energy += wgt * acc;
       if (p.pair_partials != nullptr) {

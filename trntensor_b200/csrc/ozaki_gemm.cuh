@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                      (p.strideC % 4 == 0);
     uint32_t round = 0;
     for (long long w = blockIdx.x; w < n_tiles; w += gridDim.x, ++round) {
-      if (!mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)) break;
+      if (!group_all<32 * kEpiWarps>(mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)))
+        break;
       tc_fence_after();
       const Tile t = tile_decode(w, p);
       const int bA = p.shared_A ? 0 : t.b;
