@@ -60,6 +60,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ao2mo", action="store_true", help="skip the AO->MO config 3 leg")
+    ap.add_argument("--ao2mo-only", action="store_true",
+                    help="run only the AO->MO leg (prints its JSON object)")
+    ap.add_argument("--ao-naux", type=int, default=None,
+                    help="override naux of the AO->MO leg (profiling captures)")
     ap.add_argument("--nocc", type=int, default=None,
                     help="override nocc (same tile shapes, fewer pairs; for profiling captures)")
     args = ap.parse_args()
@@ -332,7 +336,7 @@ def measure_ao2mo(args, rank, world, local):
 
     lib = _lib.load()
     dev = torch.device("cuda", local)
-    c = AO_CONFIG
+    c = dict(AO_CONFIG, naux=args.ao_naux or AO_CONFIG["naux"])
     nbf, nocc, nvir, naux = c["nbf"], c["nocc"], c["nvir"], c["naux"]
     eri, co, cv = ao2mo_inputs(nbf, nocc, nvir, naux, seed=0, device=dev)
     p0, p1 = distributed.aux_slab(naux, rank, world)
@@ -578,6 +582,10 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.ao2mo_only:
+            res = measure_ao2mo(args, rank, world, local)
+            if rank == 0:
+                print(json.dumps({"ao2mo": res}), flush=True)
         else:
             run_ours(args, rank, world, local)
     finally:

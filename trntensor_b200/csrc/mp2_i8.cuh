@@ -298,8 +298,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < 16; ++k) {
           const int b = t.b0 + c + k;
           if (arow && b < p.nvir && a <= b) {
-            const float den = eija - __ldg(p.eps_vir + b);
-            float v = 2.f * (x[k] * x[k] - x[k] * y[k] + y[k] * y[k]) / den;
+            // 1/den by the hardware reciprocal (relative error ~1e-7,
+            // unbiased at the level the energy tolerance cares about)
+            const float inv = __frcp_rn(eija - __ldg(p.eps_vir + b));
+            float v = 2.f * (x[k] * x[k] - x[k] * y[k] + y[k] * y[k]) * inv;
             if (a == b) v *= 0.5f;
             part += v;
           }
