@@ -292,10 +292,31 @@ __global__ void __launch_bounds__(kSplitThreads)
   }
 }
 
-__global__ void __launch_bounds__(kSplitThreads)
+__device__ __forceinline__ void slice4(const float (&v)[4], const float (&inv)[4], uint32_t& w1,
+                                       uint32_t& w2, uint32_t& w3) {
+  w1 = w2 = w3 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float x = v[j] * inv[j];
+    const float d1 = rintf(x);
+    const float r1 = (x - d1) * 128.f;
+    const float d2 = rintf(r1);
+    const float d3 = rintf((r1 - d2) * 128.f);
+    w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * j);
+    w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * j);
+    w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * j);
+  }
+}
+
+// Loads of kSliceRows rows are issued before any arithmetic so that each
+// thread keeps several 16-byte reads in flight.
+constexpr int kSliceRows = 2;
+
+__global__ void __launch_bounds__(kSplitThreads, 3)
     slice_kernel(const float* __restrict__ X, long long ldx, long long bsx, int batch, int K, int N,
                  int npad, const float* __restrict__ S, int8_t* __restrict__ Q) {
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  constexpr int kWarps = kSplitThreads / 32;
   const int ncb = (npad + kSplitCols - 1) / kSplitCols;
   const long long plane = (long long)batch * K * npad;
   const bool vec = (ldx % 4 == 0) && (bsx % 4 == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
@@ -312,27 +333,25 @@ __global__ void __launch_bounds__(kSplitThreads)
       inv[j] = sc > 0.f ? 1.0f / sc : 0.f;  // exact: sc is a power of two
     }
     int8_t* q1 = Q + (long long)b * K * npad + n;
-#pragma unroll 4
-    for (int k = wp; k < K; k += kSplitThreads / 32) {
-      float v[4];
-      if (nvalid > 0) load4(xc + (long long)k * ldx, vec, nvalid, v);
-      else v[0] = v[1] = v[2] = v[3] = 0.f;
-      uint32_t w1 = 0, w2 = 0, w3 = 0;
+    for (int k0 = wp; k0 < K; k0 += kWarps * kSliceRows) {
+      float v[kSliceRows][4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float x = v[j] * inv[j];
-        const float d1 = rintf(x);
-        const float r1 = (x - d1) * 128.f;
-        const float d2 = rintf(r1);
-        const float d3 = rintf((r1 - d2) * 128.f);
-        w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * j);
-        w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * j);
-        w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * j);
+      for (int r = 0; r < kSliceRows; ++r) {
+        const int k = k0 + r * kWarps;
+        if (k < K && nvalid > 0) load4(xc + (long long)k * ldx, vec, nvalid, v[r]);
+        else v[r][0] = v[r][1] = v[r][2] = v[r][3] = 0.f;
       }
-      const long long o = (long long)k * npad;
-      *reinterpret_cast<uint32_t*>(q1 + o) = w1;
-      *reinterpret_cast<uint32_t*>(q1 + o + plane) = w2;
-      *reinterpret_cast<uint32_t*>(q1 + o + 2 * plane) = w3;
+#pragma unroll
+      for (int r = 0; r < kSliceRows; ++r) {
+        const int k = k0 + r * kWarps;
+        if (k >= K) break;
+        uint32_t w1, w2, w3;
+        slice4(v[r], inv, w1, w2, w3);
+        const long long o = (long long)k * npad;
+        *reinterpret_cast<uint32_t*>(q1 + o) = w1;
+        *reinterpret_cast<uint32_t*>(q1 + o + plane) = w2;
+        *reinterpret_cast<uint32_t*>(q1 + o + 2 * plane) = w3;
+      }
     }
   }
 }
