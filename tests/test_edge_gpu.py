@@ -1,0 +1,91 @@
+"""Edge cases of the device path against the oracle: minimal and ragged
+sizes (one past every tile edge), non-contiguous / low-precision / mixed
+device inputs, empty inputs."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import trntensor_b200 as tt
+from oracle import oracle
+from trntensor_b200.inputs import mp2_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    return abs(float(a) - float(b)) / max(abs(float(b)), 1e-300)
+
+
+@pytest.mark.parametrize(
+    "shape",
+    [(1, 1, 1), (1, 5, 3), (2, 1, 7), (3, 129, 65), (2, 128, 64), (4, 257, 130), (1, 300, 1),
+     (7, 33, 200)],
+)
+def test_mp2_shapes(cuda_ok, shape):
+    B, eo, ev = mp2_inputs(*shape, seed=sum(shape))
+    ref, part = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
+    e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
+    assert rel(e.item(), ref) <= 2e-6
+    e64 = tt.mp2_energy(B.double().cuda(), eo.double().cuda(), ev.double().cuda())
+    assert rel(e64.item(), ref) <= 1e-12
+    p = tt.mp2_pair_energies(B.cuda(), eo.cuda(), ev.cuda()).cpu().numpy()
+    np.testing.assert_allclose(p, part, rtol=1e-5, atol=1e-7 * np.abs(part).max())
+
+
+def test_mp2_input_forms(cuda_ok):
+    B, eo, ev = mp2_inputs(5, 140, 90, seed=3)
+    ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
+    # non-contiguous view of the same values
+    Bt = B.transpose(1, 2).contiguous().transpose(1, 2)
+    assert not Bt.is_contiguous()
+    assert rel(tt.mp2_energy(Bt.cuda(), eo.cuda(), ev.cuda()).item(), ref) <= 2e-6
+    # eps on the host, B on the device; fp64 eps with fp32 B
+    assert rel(tt.mp2_energy(B.cuda(), eo.double(), ev.double()).item(), ref) <= 2e-6
+    # bf16 input: computed in fp32 on the bf16 values, returned as bf16
+    Bb = B.bfloat16()
+    refb, _ = oracle.mp2_energy_fp64(Bb.float().numpy(), eo.numpy(), ev.numpy())
+    eb = tt.mp2_energy(Bb.cuda(), eo.cuda(), ev.cuda())
+    assert eb.dtype == torch.bfloat16 and rel(eb.float().item(), refb) <= 1e-2
+    # precision="kahan" on fp32 returns fp32 but computes in fp64
+    ek = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda(), precision="kahan")
+    assert ek.dtype == torch.float32 and rel(ek.item(), ref) <= 1e-7
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1, 1), (1, 1, 2, 3), (129, 2, 130, 5), (64, 63, 1, 17),
+                                   (130, 129, 129, 1)])
+def test_ao2mo_shapes(cuda_ok, shape):
+    nbf, nocc, nvir, naux = shape
+    g = torch.Generator().manual_seed(sum(shape))
+    eri = torch.randn(nbf, nbf, naux, generator=g) * 0.1
+    co = torch.randn(nbf, nocc, generator=g)
+    cv = torch.randn(nbf, nvir, generator=g)
+    ref, _ = oracle.ao_to_mo_two_step(eri.double().numpy(), co.double().numpy(),
+                                      cv.double().numpy())
+    for B, tol in ((tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda()), 1e-5),
+                   (tt.ao_to_mo_transform(eri.double().cuda(), co.double().cuda(),
+                                          cv.double().cuda()), 1e-12)):
+        got = B.cpu().double().numpy()
+        assert got.shape == ref.shape
+        assert np.abs(got - ref).max() <= tol * np.abs(ref).max()
+
+
+def test_empty_inputs(cuda_ok):
+    e = tt.mp2_energy(torch.zeros(0, 4, 5, device="cuda"), torch.zeros(0, device="cuda"),
+                      torch.zeros(4, device="cuda"))
+    assert e.item() == 0.0 and e.device.type == "cuda"
+    B = tt.ao_to_mo_transform(torch.zeros(4, 4, 3, device="cuda"), torch.zeros(4, 0, device="cuda"),
+                              torch.zeros(4, 2, device="cuda"))
+    assert B.shape == (0, 2, 3)
+
+
+def test_zero_rows_are_safe(cuda_ok):
+    """All-zero B rows get scale 0 and contribute nothing (no NaN)."""
+    B, eo, ev = mp2_inputs(3, 150, 40, seed=1)
+    B[1] = 0
+    B[0, 7] = 0
+    ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
+    e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
+    assert np.isfinite(e.item()) and rel(e.item(), ref) <= 2e-6
