@@ -106,3 +106,38 @@ def test_tensor_core_vs_cuda_core(cuda_ok, shape):
     simt = _cuda_ao_to_mo_transform(eri, co, cv, kernel="simt").cpu().numpy()
     assert max_rel(tc, ref) <= TOL_F32
     assert max_rel(simt, ref) <= TOL_F32
+
+
+def test_einsum_routes_ao2mo_pattern(golden, cuda_ok):
+    """trntensor.einsum("mi,na,mnP->iaP") on CUDA operands runs the two-step
+    transform (the reference's greedy plan would build the (m,i,n,a) outer product)."""
+    eri, co, cv = ao2mo_inputs(128, 16, 112, 384, seed=0)
+    ref, _ = oracle.ao_to_mo_two_step(eri.double().numpy(), co.double().numpy(),
+                                      cv.double().numpy())
+    import sys
+
+    te = sys.modules["trntensor_b200.einsum"]
+
+    calls = []
+    orig = te._execute_path
+    te._execute_path = lambda *a: calls.append(a) or orig(*a)  # noqa: E731
+    try:
+        got = tt.einsum("mi,na,mnP->iaP", co.cuda(), cv.cuda(), eri.cuda())
+    finally:
+        te._execute_path = orig
+    assert not calls, "the generic greedy path ran instead of the AO->MO transform"
+    assert max_rel(got.cpu().numpy(), ref) <= TOL_F32
+    got2 = tt.einsum("xq,xyR,yb->qbR", co.cuda(), eri.cuda(), cv.cuda())
+    assert max_rel(got2.cpu().numpy(), ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("name", ["ao_kat_compose", "ao_kat_pipeline"])
+def test_df_mp2_pipeline(golden, cuda_ok, name):
+    eri, co, cv, eo, ev = ao_case_inputs(golden, name)
+    ref = float(golden[f"{name}/e_fp64"])
+    e = tt.df_mp2_energy(eri, co, cv, eo, ev)
+    assert e.device.type == "cpu" and abs(e.item() - ref) / abs(ref) <= 1e-5
+    e2, pairs = tt.df_mp2_energy(eri.cuda(), co.cuda(), cv.cuda(), eo.cuda(), ev.cuda(),
+                                 return_pairs=True)
+    assert pairs.shape == (co.shape[1], co.shape[1])
+    assert abs(pairs.sum().item() - ref) / abs(ref) <= 1e-5

@@ -202,3 +202,16 @@ class TestCAbi:
                                      null, None) == 2
         assert lib.tt_mp2_energy_f32(null, null, null, 4, 4, 4, 0, 10, null, 8, null, None,
                                      null, None) == 4
+
+
+def test_ao2mo_pattern_match():
+    from trntensor_b200.einsum import _ao2mo_roles
+
+    e, co, cv = torch.randn(4, 4, 3), torch.randn(4, 2), torch.randn(4, 5)
+    assert _ao2mo_roles("mi,na,mnP->iaP", (co, cv, e)) == (2, 0, 1)
+    assert _ao2mo_roles("xq,mnP,yb->qbP".replace("mnP", "xyP"), (co, e, cv)) == (1, 0, 2)
+    assert _ao2mo_roles("mi,na,mnP->aiP", (co, cv, e)) is None
+    assert _ao2mo_roles("ij,jk,kl->il", (co, co, co)) is None
+    # on CPU the generic path still runs (and agrees with torch.einsum)
+    torch.testing.assert_close(tt.einsum("mi,na,mnP->iaP", co, cv, e),
+                               torch.einsum("mi,na,mnP->iaP", co, cv, e))

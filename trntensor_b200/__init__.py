@@ -27,7 +27,7 @@ from .plan import (
     plan_cache_info,
     plan_contraction,
 )
-from .quantum import ao_to_mo_transform, mp2_energy, mp2_pair_energies
+from .quantum import ao_to_mo_transform, df_mp2_energy, mp2_energy, mp2_pair_energies
 
 __all__ = [
     "einsum",
@@ -51,4 +51,5 @@ __all__ = [
     "mp2_energy",
     "ao_to_mo_transform",
     "mp2_pair_energies",
+    "df_mp2_energy",
 ]

@@ -60,7 +60,46 @@ def einsum(
     return result
 
 
+def _ao2mo_roles(subscripts: str, operands: tuple):
+    """Match the 3-operand AO->MO transform "mi,na,mnP->iaP" (any letters).
+
+    Returns (eri_index, occ_index, vir_index) into ``operands`` when the
+    contraction is sum_{m,n} Cocc[m,i] Cvir[n,a] eri[m,n,P] -> out[i,a,P],
+    else None.
+    """
+    if len(operands) != 3 or "->" not in subscripts:
+        return None
+    lhs, out = subscripts.split("->")
+    terms = lhs.split(",")
+    three = [k for k, t in enumerate(terms) if len(t) == 3]
+    if len(three) != 1 or len(out) != 3 or len(set("".join(terms))) != 5:
+        return None
+    e = three[0]
+    m, n, P = terms[e]
+    occ = next((k for k, t in enumerate(terms) if k != e and len(t) == 2 and t[0] == m), None)
+    vir = next((k for k, t in enumerate(terms) if k != e and len(t) == 2 and t[0] == n), None)
+    if occ is None or vir is None or occ == vir:
+        return None
+    if out != terms[occ][1] + terms[vir][1] + P:
+        return None
+    return e, occ, vir
+
+
 def _execute(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.Tensor:
+    roles = _ao2mo_roles(subscripts, operands)
+    if (
+        roles is not None
+        and plan.precision in ("fast", "kahan")
+        and all(op.device.type == "cuda" for op in operands)
+        and all(op.dtype in (torch.float32, torch.float64) for op in operands)
+    ):
+        # The planner's greedy order would materialise the (m,i,n,a) outer
+        # product first; run the two-step tensor-core transform instead.
+        from .quantum import ao_to_mo_transform
+
+        e, occ, vir = roles
+        return ao_to_mo_transform(operands[e], operands[occ], operands[vir],
+                                  precision=plan.precision)
     if plan.precision == "kahan":
         dt = operands[0].dtype if operands else torch.float32
         return torch.einsum(subscripts, *(op.to(torch.float64) for op in operands)).to(dt)

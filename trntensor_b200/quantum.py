@@ -114,3 +114,32 @@ def ao_to_mo_transform(
 
     out = _cuda_ao_to_mo_transform(eri, C_occ, C_vir, precision=precision)
     return out.to(device=eri.device, dtype=eri.dtype)
+
+
+def df_mp2_energy(
+    eri: torch.Tensor,
+    C_occ: torch.Tensor,
+    C_vir: torch.Tensor,
+    eps_occ: torch.Tensor,
+    eps_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+    return_pairs: bool = False,
+):
+    """DF-MP2 energy from AO integrals: ``mp2_energy(ao_to_mo_transform(...))``.
+
+    The composed workload of the reference's tests
+    (trntensor tests/test_quantum.py:77-93, tests/test_nki_kernels.py:178-196):
+    B stays in device memory between the two steps (the B200 counterpart of the
+    reference's XLA residency). With ``return_pairs=True`` returns
+    ``(E, E_ij)`` where ``E_ij`` is the (nocc, nocc) fp64 pair-energy matrix.
+    """
+    B = ao_to_mo_transform(
+        eri.cuda() if eri.device.type == "cpu" else eri,
+        C_occ, C_vir, precision=precision,
+    )
+    if return_pairs:
+        pairs = mp2_pair_energies(B, eps_occ, eps_vir, precision=precision)
+        e = pairs.sum().to(dtype=eri.dtype)
+        return e.to(eri.device), pairs.to(eri.device)
+    return mp2_energy(B, eps_occ, eps_vir, precision=precision).to(eri.device)
