@@ -170,6 +170,28 @@ int tt_ao2mo_f64(const double* eri, const double* C_occ, const double* C_vir, in
                  int nocc, int nvir, int naux, void* workspace, size_t workspace_bytes,
                  double* B_out, void* stream);
 
+/* --------------------------------------------------------------- GEMM */
+
+/* Workspace bytes for tt_gemm_f32 (int8 slices + scales of both operands). */
+size_t tt_gemm_workspace_bytes(int M, int N, int K, int batch, int a_kmajor, int b_kmajor);
+
+/*
+ * C[b] = A[b] . B[b] for b < batch, fp32 in and out, on int8 tensor cores
+ * (Ozaki splitting: per-row / per-column power-of-two scales along K, three
+ * int8 slices, six exact int32-accumulated slice GEMMs; accuracy at the fp32
+ * level, error ~1e-7 relative to the operands' magnitudes).
+ * A is M x K: a_kmajor = 1 -> stored (M, K) row-major, 0 -> stored (K, M).
+ * B is K x N: b_kmajor = 1 -> stored (N, K) row-major, 0 -> stored (K, N).
+ * strideA/B/C: elements between batches (A/B stride must equal the operand
+ * size; C stride >= M*N). C is (M, N) row-major per batch.
+ * Serves einsum's matmul / bmm strategies (trntensor/einsum.py:129-148,
+ * trntensor/nki/dispatch.py:187-237 nki_matmul and 339-387
+ * nki_batched_matmul).
+ */
+int tt_gemm_f32(const float* A, int a_kmajor, long long strideA, const float* B, int b_kmajor,
+                long long strideB, float* C, long long strideC, int M, int N, int K, int batch,
+                void* workspace, size_t workspace_bytes, int* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,7 +14,8 @@ int setup(int dev) {
   return once_per_device(g_flags, g_ok, dev, [dev]() -> int {
     if (cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return TT_ERR_CUDA;
-    if (cudaFuncSetAttribute(oz::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(oz::gemm_kernel<false, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              oz::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
     return TT_OK;
@@ -85,7 +86,7 @@ int oz_gemm(const int8_t* QA, const float* SA, int mpad, int batchA, const int8_
   p.err = err;
   const long long tiles = (long long)p.tiles_m * p.tiles_n * batch;
   const int grid = (int)(tiles < sms ? tiles : sms);
-  oz::gemm_kernel<<<grid, oz::kThreads, oz::kSmemBytes, s>>>(ma, mb, p);
+  oz::gemm_kernel<false, false><<<grid, oz::kThreads, oz::kSmemBytes, s>>>(ma, mb, p);
   return cuda_status(cudaGetLastError());
 }
 

@@ -102,7 +102,7 @@ __device__ __forceinline__ float level_combine(int l2, int l3, int l4) {
   return (float)l2 + (float)l3 * (1.0f / 128.0f) + (float)l4 * (1.0f / 16384.0f);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+static __global__ void __launch_bounds__(kThreads, 1)
     energy_kernel(const __grid_constant__ CUtensorMap mapQ, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Every step is exact in fp32 (power-of-two scaling, Sterbenz subtraction).
 __device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
 
-__global__ void split_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+static __global__ void split_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
                              float* __restrict__ scale, long long rows, int cols, int cols_pad) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);

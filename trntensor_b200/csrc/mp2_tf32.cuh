@@ -97,7 +97,7 @@ __device__ inline Item item_decode(long long w, const Params& p) {
   return it;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+static __global__ void __launch_bounds__(kThreads, 1)
     energy_kernel(const __grid_constant__ CUtensorMap mapA_hi,
                   const __grid_constant__ CUtensorMap mapA_lo,
                   const __grid_constant__ CUtensorMap mapB_hi,

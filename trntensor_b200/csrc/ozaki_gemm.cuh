@@ -57,6 +57,10 @@ __device__ inline Tile tile_decode(long long w, const Params& p) {
   return t;
 }
 
+// AK / BK: operand stored K-major (rows of 64 k bytes per stage, 64B swizzle,
+// coordinates (k, mn, batch, slice)) instead of MN-major (128 mn bytes per
+// k row, 128B swizzle, coordinates (mn, k, batch, slice)).
+template <bool AK, bool BK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                 Params p) {
@@ -110,8 +114,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* st = smem + s * kStageBytes;
           mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_4d(st, &mapA, &full[s], t.m0, kc * kKC, bA, 0);
-          tma_load_4d(st + kOperandBytes, &mapB, &full[s], t.n0, kc * kKC, t.b, 0);
+          if (AK) tma_load_4d(st, &mapA, &full[s], kc * kKC, t.m0, bA, 0);
+          else tma_load_4d(st, &mapA, &full[s], t.m0, kc * kKC, bA, 0);
+          if (BK) tma_load_4d(st + kOperandBytes, &mapB, &full[s], kc * kKC, t.n0, t.b, 0);
+          else tma_load_4d(st + kOperandBytes, &mapB, &full[s], t.n0, kc * kKC, t.b, 0);
         }
       }
       const uint32_t issued = it;
@@ -120,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_s8(kTile, kTile, 1, 1);
+      constexpr uint32_t idesc = idesc_s8(kTile, kTile, AK ? 0 : 1, BK ? 0 : 1);
       uint32_t it = 0, round = 0;
       bool ok = true;
       for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x, ++round) {
@@ -141,8 +147,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint64_t a[3], b[3];
 #pragma unroll
             for (int t = 0; t < 3; ++t) {
-              a[t] = smem_desc(sa + t * kSliceTile + ks * 4096, 8192, 1024, 2);
-              b[t] = smem_desc(sb + t * kSliceTile + ks * 4096, 8192, 1024, 2);
+              // K-major: 64-byte rows, 8-row groups 512 B apart, k advances 32 B.
+              // MN-major: 8 k-rows of 128 B per 1 KB atom, 32 k = 4 atoms.
+              a[t] = AK ? smem_desc(sa + t * kSliceTile + ks * 32, 16, 512, 4)
+                        : smem_desc(sa + t * kSliceTile + ks * 4096, 8192, 1024, 2);
+              b[t] = BK ? smem_desc(sb + t * kSliceTile + ks * 32, 16, 512, 4)
+                        : smem_desc(sb + t * kSliceTile + ks * 4096, 8192, 1024, 2);
             }
             const uint32_t first = (kc | ks) != 0;
             mma_i8_fill(tmem + 0 * kTile, a[0], b[0], idesc, first);
@@ -256,7 +266,7 @@ __device__ __forceinline__ void load4(const float* xc, bool vec, int nvalid, flo
   }
 }
 
-__global__ void __launch_bounds__(kSplitThreads)
+static __global__ void __launch_bounds__(kSplitThreads)
     colmax_kernel(const float* __restrict__ X, long long ldx, long long bsx, int batch, int K,
                   int N, int npad, float* __restrict__ S) {
   __shared__ float red[kSplitThreads / 32][kSplitCols];
@@ -312,7 +322,7 @@ __device__ __forceinline__ void slice4(const float (&v)[4], const float (&inv)[4
 // thread keeps several 16-byte reads in flight.
 constexpr int kSliceRows = 2;
 
-__global__ void __launch_bounds__(kSplitThreads, 3)
+static __global__ void __launch_bounds__(kSplitThreads, 3)
     slice_kernel(const float* __restrict__ X, long long ldx, long long bsx, int batch, int K, int N,
                  int npad, const float* __restrict__ S, int8_t* __restrict__ Q) {
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;

@@ -224,3 +224,42 @@ def _cuda_ao_to_mo_transform(
     _lib.check(st, "tt_ao2mo_f32")
     _check_status(dev_status, "tt_ao2mo_f32")
     return out
+
+
+def _operand_layout(X: torch.Tensor, kmajor_if_contiguous: bool):
+    """(storage tensor, kmajor) for a 2-D/3-D operand without copying if possible."""
+    if X.is_contiguous():
+        return X, kmajor_if_contiguous
+    Xt = X.transpose(-1, -2)
+    if Xt.is_contiguous():
+        return Xt, not kmajor_if_contiguous
+    return X.contiguous(), kmajor_if_contiguous
+
+
+def _cuda_gemm(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """fp32 (batched) A @ B on int8 tensor cores (fp32-level accuracy).
+
+    A: (M, K) or (b, M, K); B: (K, N) or (b, K, N); CUDA fp32 tensors.
+    """
+    lib = _lib.load()
+    dev = A.device
+    batched = A.dim() == 3
+    M, K = int(A.shape[-2]), int(A.shape[-1])
+    N = int(B.shape[-1])
+    nb = int(A.shape[0]) if batched else 1
+    out = torch.empty((nb, M, N) if batched else (M, N), dtype=torch.float32, device=dev)
+    if out.numel() == 0:
+        return out
+    if K == 0:
+        return out.zero_()
+    As, a_k = _operand_layout(A, True)   # (M, K) row-major is K-major
+    Bs, b_k = _operand_layout(B, False)  # (K, N) row-major is N-major
+    ws_bytes = int(lib.tt_gemm_workspace_bytes(M, N, K, nb, int(a_k), int(b_k)))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    status = torch.empty((), dtype=torch.int32, device=dev)
+    st = lib.tt_gemm_f32(_ptr(As), int(a_k), M * K, _ptr(Bs), int(b_k), K * N, _ptr(out), M * N,
+                         M, N, K, nb, _ptr(ws), ws_bytes, _ptr(status),
+                         ctypes.c_void_p(_stream_handle()))
+    _lib.check(st, "tt_gemm_f32")
+    _check_status(status, "tt_gemm_f32")
+    return out

@@ -110,12 +110,28 @@ def _execute(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.T
         )
     if plan.strategy == "matmul":
         A, B = operands
-        return torch.matmul(A.T if plan.transA else A, B.T if plan.transB else B)
+        a, b = (A.T if plan.transA else A), (B.T if plan.transB else B)
+        if _tensor_core_ok(plan, a, b):
+            from .dispatch import _cuda_gemm
+
+            return _cuda_gemm(a, b)
+        return torch.matmul(a, b)
     if plan.strategy == "bmm":
+        if _tensor_core_ok(plan, *operands):
+            from .dispatch import _cuda_gemm
+
+            return _cuda_gemm(*operands)
         return torch.bmm(*operands)
     if plan.strategy == "path":
         return _execute_path(subscripts, operands, plan)
     return torch.einsum(subscripts, *operands)
+
+
+def _tensor_core_ok(plan: ContractionPlan, *ops: torch.Tensor) -> bool:
+    """matmul/bmm plans on CUDA fp32 operands run on the int8 tensor-core GEMM."""
+    return plan.backend == "cuda" and all(
+        op.device.type == "cuda" and op.dtype == torch.float32 for op in ops
+    )
 
 
 def _execute_path(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.Tensor:

@@ -180,7 +180,10 @@ def plan_contraction(
     _validate_subscripts(subscripts, operands)
     if precision not in _PRECISIONS:
         raise ValueError(f"precision must be 'fast', 'kahan', or 'dd', got {precision!r}")
-    key = (subscripts, tuple(tuple(op.shape) for op in operands), precision)
+    # The reference keys on (subscripts, shapes, precision); the device type is
+    # added because it decides the executor reported in ``plan.backend``.
+    key = (subscripts, tuple(tuple(op.shape) for op in operands), precision,
+           tuple(op.device.type for op in operands))
     hit = _PLAN_CACHE.get(key)
     if hit is not None:
         return hit
