@@ -466,6 +466,25 @@ def run_ours(args, rank, world, local):
     e_ref, _ = _cuda_mp2_energy(B.double(), eo.double(), ev.double(), pair_range=(pb, min(pe, pb + 8)))
     check_rel = abs(e_chk.item() - e_ref.item()) / abs(e_ref.item())
 
+    # fp64 path (precision="kahan"): rate on a 256-pair slice of the same workload
+    fp64 = None
+    if rank == 0:
+        Bd, eod, evd = B.double(), eo.double(), ev.double()
+        rng = (pb, min(pe, pb + 256))
+        _cuda_mp2_energy(Bd, eod, evd, pair_range=(rng[0], rng[0] + 2))
+        a64, b64 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a64.record()
+        _cuda_mp2_energy(Bd, eod, evd, pair_range=rng)
+        b64.record()
+        torch.cuda.synchronize(dev)
+        t64 = a64.elapsed_time(b64) / 1e3
+        n64 = rng[1] - rng[0]
+        fp64 = {"pairs": n64, "TFLOP_per_s": n64 * flops_per_pair(c) / t64 / 1e12,
+                "full_config_estimate_s": npairs / n64 * t64,
+                "kernel": "tt::mp2s::energy_kernel<double> (CUDA cores, fp64 throughout)"}
+        del Bd, eod, evd
+        torch.cuda.empty_cache()
+
     # roofline of the dominant kernel
     int8_peak = measure_int8_peak(dev)
     peaks = measured_peaks()
@@ -566,6 +585,7 @@ def run_ours(args, rank, world, local):
                                       f"fp64 all-reduce"},
             "energy": energy_value,
             "check": {"pairs": 8, "rel_err_vs_fp64_kernel": check_rel},
+            "fp64": fp64,
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": e2e,

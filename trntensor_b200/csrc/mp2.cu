@@ -49,6 +49,13 @@ int mp2_setup(int dev) {
     if (cudaFuncSetAttribute(mp2tf::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              mp2tf::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
+    if (cudaFuncSetAttribute(mp2s::energy_kernel<double>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mp2s::smem_bytes<double>()) != cudaSuccess ||
+        cudaFuncSetAttribute(mp2s::energy_kernel<float>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mp2s::smem_bytes<float>()) != cudaSuccess)
+      return TT_ERR_CUDA;
     if (cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev) !=
         cudaSuccess)
       return TT_ERR_CUDA;
@@ -293,9 +300,9 @@ int launch_simt(const T* B, const T* eps_occ, const T* eps_vir, int nocc, int nv
   p.energy = energy;
   p.pair_partials = pair_partials;
   const long long n_items = (pair_end - pair_begin) * (long long)(p.nblk * (p.nblk + 1) / 2);
-  const long long cap = (long long)g_num_sms[dev] * 8;
+  const long long cap = (long long)g_num_sms[dev];
   const int grid = (int)(n_items < cap ? n_items : cap);
-  mp2s::energy_kernel<T><<<grid, mp2s::kThreads, 0, s>>>(p);
+  mp2s::energy_kernel<T><<<grid, mp2s::kThreads, mp2s::smem_bytes<T>(), s>>>(p);
   return cuda_status(cudaGetLastError());
 }
 }  // namespace
