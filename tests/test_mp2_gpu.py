@@ -185,3 +185,19 @@ def test_tf32x3_diagnostic_is_biased(cuda_ok):
     e_i8, _ = _cuda_mp2_energy(B, eo, ev)
     assert rel(e_tf.item(), e64.item()) > 5e-6
     assert rel(e_i8.item(), e64.item()) < RTOL_F32
+
+
+@pytest.mark.parametrize("shape", [(5, 300, 100), (4, 257, 70), (3, 128, 64), (7, 640, 200)])
+def test_paired_sm_kernel(cuda_ok, shape, monkeypatch):
+    """The opt-in cta_group::2 kernel (TRNTENSOR_B200_MP2_2SM=1) gives the
+    same energies and pair energies as the fp64 oracle."""
+    B, eo, ev = mp2_inputs(*shape, seed=sum(shape))
+    ref, part = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
+    monkeypatch.setenv("TRNTENSOR_B200_MP2_2SM", "1")
+    e, p = _cuda_mp2_energy(B, eo, ev, return_partials=True)
+    assert rel(e.item(), ref) <= RTOL_F32
+    np.testing.assert_allclose(p.cpu().numpy(), part, rtol=1e-5, atol=1e-7 * np.abs(part).max())
+    npairs = shape[0] * (shape[0] + 1) // 2
+    e1, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(1, npairs))
+    e0, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(0, 1))
+    assert rel(e0.item() + e1.item(), ref) <= RTOL_F32

@@ -2,7 +2,10 @@
 // (the fp32 path), the 3xTF32 tensor-core kernel (kept as a diagnostic),
 // fp64 and fp32 CUDA-core kernels, and the operand splits they consume.
 #include "common.cuh"
+
+#include <cstdlib>
 #include "mp2_i8.cuh"
+#include "mp2_i8_2sm.cuh"
 #include "mp2_simt.cuh"
 #include "mp2_tf32.cuh"
 
@@ -46,6 +49,9 @@ int mp2_setup(int dev) {
     if (cudaFuncSetAttribute(mp2::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              mp2::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
+    if (cudaFuncSetAttribute(mp2x2::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mp2x2::kSmemBytes) != cudaSuccess)
+      return TT_ERR_CUDA;
     if (cudaFuncSetAttribute(mp2tf::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              mp2tf::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
@@ -61,6 +67,14 @@ int mp2_setup(int dev) {
       return TT_ERR_CUDA;
     return TT_OK;
   });
+}
+
+// TRNTENSOR_B200_MP2_2SM=1 selects the paired-SM (cta_group::2) kernel;
+// the one-SM kernel is the default (faster on B200, see mp2_i8_2sm.cuh).
+// Read on every call so that callers and tests can switch between them.
+bool use_paired_kernel() {
+  const char* e = std::getenv("TRNTENSOR_B200_MP2_2SM");
+  return e != nullptr && e[0] == '1';
 }
 
 inline int naux_padded(int naux) { return (naux + 15) / 16 * 16; }     // tf32 split
@@ -150,14 +164,18 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
     TT_CUDA(cudaMemsetAsync(pair_partials, 0, sizeof(double) * (size_t)nocc * nocc, s));
   if (pair_end == pair_begin) return TT_OK;
   // Slices as a 4-D byte tensor (aux, vir, occ, slice), innermost first;
-  // one box = 64 aux x 128 rows x all 3 slices, 64B swizzle.
-  CUtensorMap mq;
+  // one box = 64 aux x 128 rows (64 for the paired kernel's B half) x all 3
+  // slices, 64B swizzle.
+  CUtensorMap mq, mq_half;
   const uint64_t rows = (uint64_t)nocc * nvir;
   const uint64_t dims[4] = {(uint64_t)naux_pad, (uint64_t)nvir, (uint64_t)nocc, 3};
   const uint64_t strides[3] = {(uint64_t)naux_pad, (uint64_t)naux_pad * nvir,
                                (uint64_t)naux_pad * rows};
   const uint32_t box[4] = {(uint32_t)mp2::kKC, (uint32_t)mp2::kBlk, 1, 3};
+  const uint32_t box_half[4] = {(uint32_t)mp2::kKC, (uint32_t)mp2::kBlk / 2, 1, 3};
   if (encode_tmap(&mq, Q, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_DATA_TYPE_UINT8) ||
+      encode_tmap(&mq_half, Q, 4, dims, strides, box_half, CU_TENSOR_MAP_SWIZZLE_64B,
                   CU_TENSOR_MAP_DATA_TYPE_UINT8))
     return TT_ERR_TMA;
   mp2::Params p;
@@ -174,6 +192,15 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
   p.pair_partials = pair_partials;
   p.err = dev_status;
   p.prof = g_mp2_prof;
+  if (use_paired_kernel()) {
+    // pairs of SMs: one cluster of 2 CTAs per 256 x 128 strip
+    const long long n_items =
+        (pair_end - pair_begin) * (long long)mp2x2::items_per_pair(p.nblk);
+    const long long ncl_max = g_num_sms[dev] / 2;
+    const int ncl = (int)(n_items < ncl_max ? n_items : ncl_max);
+    mp2x2::energy_kernel<<<2 * ncl, mp2x2::kThreads, mp2x2::kSmemBytes, s>>>(mq, mq_half, p);
+    return cuda_status(cudaGetLastError());
+  }
   const long long n_items = (pair_end - pair_begin) * (long long)(p.nblk * (p.nblk + 1) / 2);
   const int grid = (int)(n_items < g_num_sms[dev] ? n_items : g_num_sms[dev]);
   mp2::energy_kernel<<<grid, mp2::kThreads, mp2::kSmemBytes, s>>>(mq, p);
