@@ -141,3 +141,24 @@ def test_df_mp2_pipeline(golden, cuda_ok, name):
                                  return_pairs=True)
     assert pairs.shape == (co.shape[1], co.shape[1])
     assert abs(pairs.sum().item() - ref) / abs(ref) <= 1e-5
+
+
+@pytest.mark.parametrize("shape", [(128, 16, 112, 384), (200, 10, 20, 24), (130, 129, 129, 7),
+                                   (256, 130, 100, 64)])
+def test_step1_on_chip_split_matches_preslice(cuda_ok, shape, monkeypatch):
+    """Step 1 with eri split in shared memory (default) and with eri pre-split
+    in HBM (TRNTENSOR_B200_AO2MO_PRESLICE=1) both match fp64; naux = 7 makes
+    eri's row stride unaligned, which selects the pre-split path."""
+    from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
+
+    nbf, nocc, nvir, naux = shape
+    g = torch.Generator().manual_seed(sum(shape))
+    eri = torch.randn(nbf, nbf, naux, generator=g) * 0.1
+    co = torch.randn(nbf, nocc, generator=g)
+    cv = torch.randn(nbf, nvir, generator=g)
+    ref = _cuda_ao_to_mo_transform(eri.double(), co.double(), cv.double()).cpu().numpy()
+    a = _cuda_ao_to_mo_transform(eri, co, cv).cpu().numpy()
+    monkeypatch.setenv("TRNTENSOR_B200_AO2MO_PRESLICE", "1")
+    b = _cuda_ao_to_mo_transform(eri, co, cv).cpu().numpy()
+    assert max_rel(a, ref) <= TOL_F32
+    assert max_rel(b, ref) <= TOL_F32

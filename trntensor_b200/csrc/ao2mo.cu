@@ -2,6 +2,9 @@
 #include "ao2mo_simt.cuh"
 #include "common.cuh"
 #include "ozaki_gemm.cuh"
+#include "ozaki_gemm_cvt.cuh"
+
+#include <cstdlib>
 
 namespace tt {
 namespace {
@@ -13,6 +16,9 @@ int g_sms[kMaxDevices];
 int setup(int dev) {
   return once_per_device(g_flags, g_ok, dev, [dev]() -> int {
     if (cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return TT_ERR_CUDA;
+    if (cudaFuncSetAttribute(ozc::gemm_cvt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             ozc::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
     if (cudaFuncSetAttribute(oz::gemm_kernel<false, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -177,12 +183,45 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
   // Column-scaled int8 slices of the three operands of step 1 and of C_vir.
   if ((st = split_cols(C_occ, nocc, 0, 1, nbf, nocc, po, qo, so, s, sms))) return st;
   if ((st = split_cols(C_vir, nvir, 0, 1, nbf, nvir, pv, qv, sv, s, sms))) return st;
-  if ((st = split_cols(eri, (long long)nbf * naux, 0, 1, nbf, nbf * naux, pe, qe, se, s, sms)))
-    return st;
-  // step 1: inter[i][(n,P)] = sum_m C_occ[m][i] eri[m][(n,P)]
-  if ((st = oz_gemm(qo, so, po, 1, qe, se, pe, 1, nocc, nbf * naux, nbf, inter,
-                    (long long)nbf * naux, 0, dev_status, s, sms)))
-    return st;
+  const long long ncol = (long long)nbf * naux;
+  const char* pre = std::getenv("TRNTENSOR_B200_AO2MO_PRESLICE");
+  const bool preslice = (pre != nullptr && pre[0] == '1') || (ncol % 4 != 0) || !aligned16(eri);
+  if (preslice) {
+    // eri split into int8 slices in HBM, then the generic slice GEMM
+    if ((st = split_cols(eri, ncol, 0, 1, nbf, nbf * naux, pe, qe, se, s, sms))) return st;
+    // step 1: inter[i][(n,P)] = sum_m C_occ[m][i] eri[m][(n,P)]
+    if ((st = oz_gemm(qo, so, po, 1, qe, se, pe, 1, nocc, nbf * naux, nbf, inter, ncol, 0,
+                      dev_status, s, sms)))
+      return st;
+  } else {
+    // column scales of eri only; the GEMM splits fp32 eri tiles on chip
+    const long long nblk = (pe + oz::kSplitCols - 1) / oz::kSplitCols;
+    const int g = (int)(nblk < (long long)sms * 8 ? nblk : (long long)sms * 8);
+    oz::colmax_kernel<<<g, oz::kSplitThreads, 0, s>>>(eri, ncol, 0, 1, nbf, nbf * naux, pe, se);
+    if ((st = cuda_status(cudaGetLastError()))) return st;
+    CUtensorMap ma, mx;
+    const uint64_t xd[2] = {(uint64_t)ncol, (uint64_t)nbf};
+    const uint64_t xs[1] = {(uint64_t)ncol * 4};
+    const uint32_t xb[2] = {(uint32_t)ozc::kTile, (uint32_t)ozc::kKC};
+    if (slice_map(&ma, qo, po, nbf, 1) ||
+        encode_tmap(&mx, eri, 2, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return TT_ERR_TMA;
+    ozc::Params pc;
+    pc.sA = so;
+    pc.sX = se;
+    pc.C = inter;
+    pc.ldc = ncol;
+    pc.M = nocc;
+    pc.N = nbf * naux;
+    pc.K = nbf;
+    pc.tiles_m = (nocc + ozc::kTile - 1) / ozc::kTile;
+    pc.tiles_n = (int)((ncol + ozc::kTile - 1) / ozc::kTile);
+    pc.err = dev_status;
+    const long long tiles = (long long)pc.tiles_m * pc.tiles_n;
+    const int grid = (int)(tiles < sms ? tiles : sms);
+    ozc::gemm_cvt_kernel<<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
+    if ((st = cuda_status(cudaGetLastError()))) return st;
+  }
   // slices of inter[i] (K = n, N = P), scales per (i, P)
   if ((st = split_cols(inter, naux, (long long)nbf * naux, nocc, nbf, naux, pa, qi, si, s, sms)))
     return st;

@@ -1,0 +1,296 @@
+// Step 1 of the AO->MO transform with the B operand converted on chip:
+//   C[m][n] = sum_k A[k][m] X[k][n]
+// A: int8 Ozaki slices of C_occ (MN-major, as in ozaki_gemm.cuh);
+// X: fp32 rows (eri viewed as nbf x nbf*naux), read once by TMA in
+//    64 x 128 tiles and split in shared memory, with the column scales s_n
+//    (max over all k) computed beforehand by colmax_kernel.
+// This removes the separate slice pass and its 3 bytes/element round trip
+// through HBM. Per stage: TMA writes the fp32 tile (32 KB) and the A slices
+// (24 KB); eight converter warps read the tile (lane l: one float4 of a
+// row, a warp reads a whole row), agree on a named barrier, overwrite the
+// tile in place with the three int8 slice tiles in the MN-major
+// 128B-swizzled layout the MMA descriptors expect (one 32-bit store per
+// lane and slice, a warp writes a whole 128-byte row), fence the async
+// proxy and arrive on conv[s]; the MMA thread waits on fullA[s] and conv[s].
+// Measured at config 3: 5.6 ms against 7.9 ms for splitting eri in HBM
+// first (slice pass 5.2 ms + slice GEMM 2.7 ms); the converter warps'
+// per-stage latency bounds it, not HBM (a variant with a separate
+// fp32 landing ring and converter-copied A tiles measured 8.7 ms).
+// Roles: warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue, 10..17 convert.
+#pragma once
+#include "ozaki_gemm.cuh"
+
+namespace tt {
+namespace ozc {
+
+using oz::kTile;  // 128
+using oz::kKC;    // 64
+using oz::level_combine;
+
+constexpr int kStages = 3;
+constexpr int kARegion = 3 * kTile * kKC;     // 24 KB of A slices
+constexpr int kBRegion = kTile * kKC * 4;     // 32 KB fp32 tile, later 24 KB of slices
+constexpr int kStageBytes = kARegion + kBRegion;
+constexpr int kEpiWarps = 8;
+constexpr int kCvtWarps = 8;
+constexpr int kThreads = 64 + 32 * (kEpiWarps + kCvtWarps);
+constexpr int kHalfLd = kTile / 2 + 4;        // padded row of a half-tile output stage
+constexpr int kOutBytes = kTile * kHalfLd * 4;
+constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
+
+struct Params {
+  const float* sA;    // column scales of A (per m)
+  const float* sX;    // column scales of X (per n), from colmax_kernel
+  float* C;
+  long long ldc;
+  int M, N, K;
+  int tiles_m, tiles_n;
+  int* err;
+};
+
+static __global__ void __launch_bounds__(kThreads, 1)
+    gemm_cvt_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX,
+                    Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  float* ostage = (float*)(smem + kStages * kStageBytes);
+  uint64_t* fullA = (uint64_t*)(smem + kStages * kStageBytes + kOutBytes);
+  uint64_t* fullB = fullA + kStages;
+  uint64_t* conv = fullB + kStages;
+  uint64_t* empty = conv + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* final_bar = acc_empty + 1;
+  uint32_t* tmem_slot = (uint32_t*)(final_bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long n_tiles = (long long)p.tiles_m * p.tiles_n;
+  const int nkc = (p.K + kKC - 1) / kKC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&fullA[s], 1);
+      mbar_init(&fullB[s], 1);
+      mbar_init(&conv[s], kCvtWarps);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 32 * kEpiWarps);
+    mbar_init(final_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&mapA);
+    tma_prefetch_desc(&mapX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto tile_of = [&](long long w, int& m0, int& n0) {
+    n0 = (int)(w / p.tiles_m) * kTile;  // consecutive tiles share the X columns
+    m0 = (int)(w % p.tiles_m) * kTile;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
+        int m0, n0;
+        tile_of(w, m0, n0);
+        for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&fullA[s], kARegion);
+          tma_load_4d(st, &mapA, &fullA[s], m0, kc * kKC, 0, 0);
+          mbar_arrive_expect_tx(&fullB[s], kBRegion);
+          tma_load_2d(st + kARegion, &mapX, &fullB[s], n0, kc * kKC);
+        }
+      }
+      const uint32_t issued = it;
+      for (uint32_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k) {
+        mbar_wait_drain(&fullA[k % kStages], (k / kStages) & 1u);
+        mbar_wait_drain(&fullB[k % kStages], (k / kStages) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8(kTile, kTile, 1, 1);
+      uint32_t it = 0, round = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x, ++round) {
+        if (!mbar_wait(acc_empty, (round & 1u) ^ 1u, p.err, kDevTimeoutAccFree)) break;
+        tc_fence_after();
+        for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(&fullA[s], ph, p.err, kDevTimeoutFull) ||
+              !mbar_wait(&conv[s], ph, p.err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + kARegion;
+#pragma unroll
+          for (int ks = 0; ks < kKC / 32; ++ks) {
+            uint64_t a[3], b[3];
+#pragma unroll
+            for (int t = 0; t < 3; ++t) {
+              a[t] = smem_desc(sa + t * oz::kSliceTile + ks * 4096, 8192, 1024, 2);
+              b[t] = smem_desc(sb + t * oz::kSliceTile + ks * 4096, 8192, 1024, 2);
+            }
+            const uint32_t first = (kc | ks) != 0;
+            mma_i8_fill(tmem + 0 * kTile, a[0], b[0], idesc, first);
+            mma_i8_use(tmem + 1 * kTile, a[0], b[1], idesc, first);
+            mma_i8_lastuse(tmem + 2 * kTile, a[0], b[2], idesc, first);
+            mma_i8_fill(tmem + 1 * kTile, a[1], b[0], idesc, 1);
+            mma_i8_lastuse(tmem + 2 * kTile, a[1], b[1], idesc, 1);
+            mma_i8(tmem + 2 * kTile, a[2], b[0], idesc, 1);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(acc_full);
+      }
+      mma_commit(final_bar);
+      mbar_wait_drain(final_bar, 0);
+    }
+  } else if (warp < 2 + kEpiWarps) {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;  // this warp's 64-column half
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+    uint32_t round = 0;
+    for (long long w = blockIdx.x; w < n_tiles; w += gridDim.x, ++round) {
+      if (!group_all<32 * kEpiWarps, 1>(mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)))
+        break;
+      tc_fence_after();
+      int m0, n0;
+      tile_of(w, m0, n0);
+      const int m = m0 + row;
+      const float sa = m < p.M ? __ldg(p.sA + m) : 0.f;
+      const int nn = p.N - n0 < kTile ? p.N - n0 : kTile;
+      // Two rounds through a half-tile stage: warps of half h drain, then
+      // all eight warps store the 128 rows x 64 columns coalesced.
+      for (int h = 0; h < 2; ++h) {
+        if (half == h) {
+          for (int c = 0; c < kTile / 2; c += 16) {
+            const int cc = h * (kTile / 2) + c;
+            int l2[16], l3[16], l4[16];
+            tmem_ld16i(lane_base + 0 * kTile + cc, l2);
+            tmem_ld16i(lane_base + 1 * kTile + cc, l3);
+            tmem_ld16i(lane_base + 2 * kTile + cc, l4);
+            tmem_ld_wait();
+            float v[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int n = n0 + cc + k;
+              const float sb = n < p.N ? __ldg(p.sX + n) : 0.f;
+              v[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
+            }
+            float4* dst = reinterpret_cast<float4*>(ostage + row * kHalfLd + c);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          }
+        }
+        tc_fence_before();
+        if (h == 1) mbar_arrive(acc_empty);  // both halves drained: TMEM is free
+        group_sync<32 * kEpiWarps, 1>();
+        const int c0 = h * (kTile / 2);
+        const int ncols = nn - c0;
+        for (int r = ew * 2 + (lane >> 4); r < kTile; r += 2 * kEpiWarps) {
+          const int mm = m0 + r;
+          if (mm >= p.M || ncols <= 0) continue;
+          float* crow = p.C + (long long)mm * p.ldc + n0 + c0;
+          const float* srow = ostage + r * kHalfLd;
+          const int l16 = lane & 15;
+          if (vec && ncols >= kTile / 2) {
+            reinterpret_cast<float4*>(crow)[l16] = reinterpret_cast<const float4*>(srow)[l16];
+          } else {
+            for (int c = l16; c < ncols && c < kTile / 2; c += 16) crow[c] = srow[c];
+          }
+        }
+        group_sync<32 * kEpiWarps, 1>();  // stage free for the next half
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- converters
+    const int cw = warp - (2 + kEpiWarps);
+    constexpr int kRows = kKC / kCvtWarps;  // 8 rows per warp and stage
+    uint32_t it = 0;
+    bool ok = true;
+    for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
+      int m0, n0;
+      tile_of(w, m0, n0);
+      float inv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int n = n0 + 4 * lane + k;
+        const float sc = n < p.N ? __ldg(p.sX + n) : 0.f;
+        inv[k] = sc > 0.f ? 1.0f / sc : 0.f;  // exact: sc is a power of two
+      }
+      for (int kc = 0; kc < nkc; ++kc, ++it) {
+        const int s = it % kStages;
+        ok = group_all<32 * kCvtWarps, 2>(
+            mbar_wait(&fullB[s], (it / kStages) & 1u, p.err, kDevTimeoutFull));
+        if (!ok) break;
+        uint8_t* tile = smem + s * kStageBytes + kARegion;
+        const float4* f = reinterpret_cast<const float4*>(tile);
+        float4 v[kRows];
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) v[j] = f[(cw + kCvtWarps * j) * (kTile / 4) + lane];
+        group_sync<32 * kCvtWarps, 2>();  // every fp32 value of the tile is read
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+          const int r = cw + kCvtWarps * j;
+          const float xs[4] = {v[j].x * inv[0], v[j].y * inv[1], v[j].z * inv[2], v[j].w * inv[3]};
+          uint32_t w1 = 0, w2 = 0, w3 = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float d1 = rintf(xs[k]);
+            const float q1 = (xs[k] - d1) * 128.f;
+            const float d2 = rintf(q1);
+            const float d3 = rintf((q1 - d2) * 128.f);
+            w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * k);
+            w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * k);
+            w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * k);
+          }
+          // MN-major SW128 atom: 8 k-rows x 128 bytes; the 16-byte chunk
+          // index (lane / 4) is XORed with (row mod 8).
+          const int off = (r >> 3) * 1024 + (r & 7) * 128 + ((((lane >> 2) ^ (r & 7))) << 4) +
+                          (lane & 3) * 4;
+          *reinterpret_cast<uint32_t*>(tile + 0 * oz::kSliceTile + off) = w1;
+          *reinterpret_cast<uint32_t*>(tile + 1 * oz::kSliceTile + off) = w2;
+          *reinterpret_cast<uint32_t*>(tile + 2 * oz::kSliceTile + off) = w3;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace ozc
+}  // namespace tt

@@ -83,18 +83,27 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 // AND of `ok` over the `nthreads` threads that use named barrier 1 (the
 // epilogue warps). Used after each bounded wait so that those warps leave
 // their loop together and never strand each other at a named barrier.
-template <int kN>
+template <int kN, int kBar = 1>
 __device__ __forceinline__ bool group_all(bool ok) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "bar.red.and.pred q, %3, %2, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)ok), "n"(kN)
+      : "r"((uint32_t)ok), "n"(kN), "n"(kBar)
       : "memory");
   return r != 0;
+}
+template <int kN, int kBar>
+__device__ __forceinline__ void group_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kBar), "n"(kN) : "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA / tensor-core reads) before signalling an mbarrier.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // --------------------------------------------------------------------- TMA
