@@ -5,17 +5,16 @@
 //    64 x 128 tiles and split in shared memory, with the column scales s_n
 //    (max over all k) computed beforehand by colmax_kernel.
 // This removes the separate slice pass and its 3 bytes/element round trip
-// through HBM. Per stage: TMA writes the fp32 tile (32 KB) and the A slices
-// (24 KB); eight converter warps read the tile (lane l: one float4 of a
-// row, a warp reads a whole row), agree on a named barrier, overwrite the
-// tile in place with the three int8 slice tiles in the MN-major
-// 128B-swizzled layout the MMA descriptors expect (one 32-bit store per
-// lane and slice, a warp writes a whole 128-byte row), fence the async
-// proxy and arrive on conv[s]; the MMA thread waits on fullA[s] and conv[s].
-// Measured at config 3: 5.6 ms against 7.9 ms for splitting eri in HBM
-// first (slice pass 5.2 ms + slice GEMM 2.7 ms); the converter warps'
-// per-stage latency bounds it, not HBM (a variant with a separate
-// fp32 landing ring and converter-copied A tiles measured 8.7 ms).
+// through HBM. Two rings in shared memory:
+//   fp32 landing ring (3 x 32 KB): one producer lane's TMA fills X tiles;
+//     converter warps read their rows (lane l: one float4 of a row, a warp
+//     reads a whole row) and release the slot at once, so the ring only has
+//     to cover HBM latency;
+//   int8 ring (2 x 48 KB): a second producer lane's TMA brings the A slice
+//     tiles; converter warps write the three B slice tiles in the MN-major
+//     128B-swizzled layout the MMA descriptors expect (one 32-bit store per
+//     lane and slice, a warp writes a whole 128-byte row), fence the async
+//     proxy and arrive on conv; the MMA thread waits on fullA and conv.
 // Roles: warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue, 10..17 convert.
 #pragma once
 #include "ozaki_gemm.cuh"
@@ -27,16 +26,18 @@ using oz::kTile;  // 128
 using oz::kKC;    // 64
 using oz::level_combine;
 
-constexpr int kStages = 3;
+constexpr int kFStages = 3;                   // fp32 landing ring (TMA -> converters)
+constexpr int kIStages = 2;                   // int8 ring (A by TMA, B by converters -> MMA)
+constexpr int kFBytes = kTile * kKC * 4;      // 32 KB fp32 tile
 constexpr int kARegion = 3 * kTile * kKC;     // 24 KB of A slices
-constexpr int kBRegion = kTile * kKC * 4;     // 32 KB fp32 tile, later 24 KB of slices
-constexpr int kStageBytes = kARegion + kBRegion;
+constexpr int kIBytes = 2 * kARegion;         // A and B slices: 48 KB
 constexpr int kEpiWarps = 8;
-constexpr int kCvtWarps = 8;
+constexpr int kCvtWarps = 8;   // (16 converter + 4 epilogue warps measured no faster)
 constexpr int kThreads = 64 + 32 * (kEpiWarps + kCvtWarps);
-constexpr int kHalfLd = kTile / 2 + 4;        // padded row of a half-tile output stage
-constexpr int kOutBytes = kTile * kHalfLd * 4;
-constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
+constexpr int kQCols = kTile / 4;             // output staged a quarter tile at a time
+constexpr int kQLd = kQCols + 4;
+constexpr int kOutBytes = kTile * kQLd * 4;
+constexpr int kSmemBytes = kFStages * kFBytes + kIStages * kIBytes + kOutBytes + 1024 + 256;
 
 struct Params {
   const float* sA;    // column scales of A (per m)
@@ -53,12 +54,15 @@ static __global__ void __launch_bounds__(kThreads, 1)
                     Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  float* ostage = (float*)(smem + kStages * kStageBytes);
-  uint64_t* fullA = (uint64_t*)(smem + kStages * kStageBytes + kOutBytes);
-  uint64_t* fullB = fullA + kStages;
-  uint64_t* conv = fullB + kStages;
-  uint64_t* empty = conv + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint8_t* fring = smem;
+  uint8_t* iring = smem + kFStages * kFBytes;
+  float* ostage = (float*)(iring + kIStages * kIBytes);
+  uint64_t* fullF = (uint64_t*)((uint8_t*)ostage + kOutBytes);
+  uint64_t* freeF = fullF + kFStages;
+  uint64_t* fullA = freeF + kFStages;
+  uint64_t* conv = fullA + kIStages;
+  uint64_t* emptyI = conv + kIStages;
+  uint64_t* acc_full = emptyI + kIStages;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* final_bar = acc_empty + 1;
   uint32_t* tmem_slot = (uint32_t*)(final_bar + 1);
@@ -68,11 +72,14 @@ static __global__ void __launch_bounds__(kThreads, 1)
   const int nkc = (p.K + kKC - 1) / kKC;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kFStages; ++s) {
+      mbar_init(&fullF[s], 1);
+      mbar_init(&freeF[s], kCvtWarps);
+    }
+    for (int s = 0; s < kIStages; ++s) {
       mbar_init(&fullA[s], 1);
-      mbar_init(&fullB[s], 1);
       mbar_init(&conv[s], kCvtWarps);
-      mbar_init(&empty[s], 1);
+      mbar_init(&emptyI[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 32 * kEpiWarps);
@@ -96,31 +103,37 @@ static __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // ----------------------------------------- producers (two lanes of warp 0)
+    // lane 0: fp32 X tiles into the landing ring; lane 16: A slice tiles into
+    // the int8 ring as soon as the MMA has released a slot.
+    if (lane == 0 || lane == 16) {
+      const bool fp32 = lane == 0;
+      const int nst = fp32 ? kFStages : kIStages;
+      uint64_t* wait_bar = fp32 ? freeF : emptyI;
+      uint64_t* fill_bar = fp32 ? fullF : fullA;
       uint32_t it = 0;
       bool ok = true;
       for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
         int m0, n0;
         tile_of(w, m0, n0);
         for (int kc = 0; kc < nkc; ++kc, ++it) {
-          const int s = it % kStages;
-          if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
+          const int s = it % nst;
+          if (!mbar_wait(&wait_bar[s], ((it / nst) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
-          uint8_t* st = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&fullA[s], kARegion);
-          tma_load_4d(st, &mapA, &fullA[s], m0, kc * kKC, 0, 0);
-          mbar_arrive_expect_tx(&fullB[s], kBRegion);
-          tma_load_2d(st + kARegion, &mapX, &fullB[s], n0, kc * kKC);
+          if (fp32) {
+            mbar_arrive_expect_tx(&fill_bar[s], kFBytes);
+            tma_load_2d(fring + s * kFBytes, &mapX, &fill_bar[s], n0, kc * kKC);
+          } else {
+            mbar_arrive_expect_tx(&fill_bar[s], kARegion);
+            tma_load_4d(iring + s * kIBytes, &mapA, &fill_bar[s], m0, kc * kKC, 0, 0);
+          }
         }
       }
       const uint32_t issued = it;
-      for (uint32_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k) {
-        mbar_wait_drain(&fullA[k % kStages], (k / kStages) & 1u);
-        mbar_wait_drain(&fullB[k % kStages], (k / kStages) & 1u);
-      }
+      for (uint32_t k = (issued > (uint32_t)nst ? issued - nst : 0); k < issued; ++k)
+        mbar_wait_drain(&fill_bar[k % nst], (k / nst) & 1u);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
@@ -132,15 +145,15 @@ static __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(acc_empty, (round & 1u) ^ 1u, p.err, kDevTimeoutAccFree)) break;
         tc_fence_after();
         for (int kc = 0; kc < nkc; ++kc, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % kIStages;
+          const uint32_t ph = (it / kIStages) & 1u;
           if (!mbar_wait(&fullA[s], ph, p.err, kDevTimeoutFull) ||
               !mbar_wait(&conv[s], ph, p.err, kDevTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sa = smem_u32(iring + s * kIBytes);
           const uint32_t sb = sa + kARegion;
 #pragma unroll
           for (int ks = 0; ks < kKC / 32; ++ks) {
@@ -158,7 +171,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
             mma_i8_lastuse(tmem + 2 * kTile, a[1], b[1], idesc, 1);
             mma_i8(tmem + 2 * kTile, a[2], b[0], idesc, 1);
           }
-          mma_commit(&empty[s]);
+          mma_commit(&emptyI[s]);
         }
         if (ok) mma_commit(acc_full);
       }
@@ -183,12 +196,14 @@ static __global__ void __launch_bounds__(kThreads, 1)
       const int m = m0 + row;
       const float sa = m < p.M ? __ldg(p.sA + m) : 0.f;
       const int nn = p.N - n0 < kTile ? p.N - n0 : kTile;
-      // Two rounds through a half-tile stage: warps of half h drain, then
-      // all eight warps store the 128 rows x 64 columns coalesced.
-      for (int h = 0; h < 2; ++h) {
-        if (half == h) {
-          for (int c = 0; c < kTile / 2; c += 16) {
-            const int cc = h * (kTile / 2) + c;
+      // Four rounds through a quarter-tile stage: the warps owning columns
+      // [32h, 32h+32) drain them, then all eight warps store 128 rows x 32
+      // columns with coalesced row segments.
+      for (int h = 0; h < 4; ++h) {
+        if (half == (h >> 1)) {
+#pragma unroll
+          for (int c = 0; c < kQCols; c += 16) {
+            const int cc = h * kQCols + c;
             int l2[16], l3[16], l4[16];
             tmem_ld16i(lane_base + 0 * kTile + cc, l2);
             tmem_ld16i(lane_base + 1 * kTile + cc, l3);
@@ -201,30 +216,31 @@ static __global__ void __launch_bounds__(kThreads, 1)
               const float sb = n < p.N ? __ldg(p.sX + n) : 0.f;
               v[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
             }
-            float4* dst = reinterpret_cast<float4*>(ostage + row * kHalfLd + c);
+            float4* dst = reinterpret_cast<float4*>(ostage + row * kQLd + c);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
           }
         }
         tc_fence_before();
-        if (h == 1) mbar_arrive(acc_empty);  // both halves drained: TMEM is free
+        if (h == 3) mbar_arrive(acc_empty);  // all columns drained: TMEM is free
         group_sync<32 * kEpiWarps, 1>();
-        const int c0 = h * (kTile / 2);
+        const int c0 = h * kQCols;
         const int ncols = nn - c0;
-        for (int r = ew * 2 + (lane >> 4); r < kTile; r += 2 * kEpiWarps) {
+        // 4 rows per warp instruction: 8 lanes x float4 = one 32-column row
+        for (int r = ew * 4 + (lane >> 3); r < kTile; r += 4 * kEpiWarps) {
           const int mm = m0 + r;
           if (mm >= p.M || ncols <= 0) continue;
           float* crow = p.C + (long long)mm * p.ldc + n0 + c0;
-          const float* srow = ostage + r * kHalfLd;
-          const int l16 = lane & 15;
-          if (vec && ncols >= kTile / 2) {
-            reinterpret_cast<float4*>(crow)[l16] = reinterpret_cast<const float4*>(srow)[l16];
+          const float* srow = ostage + r * kQLd;
+          const int l8 = lane & 7;
+          if (vec && ncols >= kQCols) {
+            reinterpret_cast<float4*>(crow)[l8] = reinterpret_cast<const float4*>(srow)[l8];
           } else {
-            for (int c = l16; c < ncols && c < kTile / 2; c += 16) crow[c] = srow[c];
+            for (int c = l8; c < ncols && c < kQCols; c += 8) crow[c] = srow[c];
           }
         }
-        group_sync<32 * kEpiWarps, 1>();  // stage free for the next half
+        group_sync<32 * kEpiWarps, 1>();  // stage free for the next quarter
       }
     }
   } else {
@@ -241,33 +257,44 @@ static __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 4; ++k) {
         const int n = n0 + 4 * lane + k;
         const float sc = n < p.N ? __ldg(p.sX + n) : 0.f;
-        inv[k] = sc > 0.f ? 1.0f / sc : 0.f;  // exact: sc is a power of two
+        inv[k] = sc > 0.f ? 16384.0f / sc : 0.f;  // exact: sc is a power of two
       }
       for (int kc = 0; kc < nkc; ++kc, ++it) {
-        const int s = it % kStages;
-        ok = group_all<32 * kCvtWarps, 2>(
-            mbar_wait(&fullB[s], (it / kStages) & 1u, p.err, kDevTimeoutFull));
-        if (!ok) break;
-        uint8_t* tile = smem + s * kStageBytes + kARegion;
-        const float4* f = reinterpret_cast<const float4*>(tile);
+        const int f = it % kFStages, s = it % kIStages;
+        if (!mbar_wait(&fullF[f], (it / kFStages) & 1u, p.err, kDevTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        const float4* src = reinterpret_cast<const float4*>(fring + f * kFBytes);
         float4 v[kRows];
 #pragma unroll
-        for (int j = 0; j < kRows; ++j) v[j] = f[(cw + kCvtWarps * j) * (kTile / 4) + lane];
-        group_sync<32 * kCvtWarps, 2>();  // every fp32 value of the tile is read
+        for (int j = 0; j < kRows; ++j) v[j] = src[(cw + kCvtWarps * j) * (kTile / 4) + lane];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&freeF[f]);  // this warp's rows are read
+        if (!mbar_wait(&emptyI[s], ((it / kIStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        uint8_t* tile = iring + s * kIBytes + kARegion;
 #pragma unroll
         for (int j = 0; j < kRows; ++j) {
           const int r = cw + kCvtWarps * j;
-          const float xs[4] = {v[j].x * inv[0], v[j].y * inv[1], v[j].z * inv[2], v[j].w * inv[3]};
+          // Y = round(x / s * 2^14) is exact in int32 (|Y| <= 127 * 2^14);
+          // its balanced base-128 digits are the slices:
+          //   q3 = ((Y + 64) & 127) - 64, Y' = (Y - q3) / 128, q2 likewise,
+          //   q1 = (Y' - q2) / 128, so x / s = q1 + q2 / 2^7 + q3 / 2^14 + O(2^-15).
+          const int Y[4] = {__float2int_rn(v[j].x * inv[0]), __float2int_rn(v[j].y * inv[1]),
+                            __float2int_rn(v[j].z * inv[2]), __float2int_rn(v[j].w * inv[3])};
           uint32_t w1 = 0, w2 = 0, w3 = 0;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const float d1 = rintf(xs[k]);
-            const float q1 = (xs[k] - d1) * 128.f;
-            const float d2 = rintf(q1);
-            const float d3 = rintf((q1 - d2) * 128.f);
-            w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * k);
-            w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * k);
-            w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * k);
+            const int d3 = ((Y[k] + 64) & 127) - 64;
+            const int y1 = (Y[k] - d3) >> 7;
+            const int d2 = ((y1 + 64) & 127) - 64;
+            const int d1 = (y1 - d2) >> 7;
+            w1 |= ((uint32_t)d1 & 0xffu) << (8 * k);
+            w2 |= ((uint32_t)d2 & 0xffu) << (8 * k);
+            w3 |= ((uint32_t)d3 & 0xffu) << (8 * k);
           }
           // MN-major SW128 atom: 8 k-rows x 128 bytes; the 16-byte chunk
           // index (lane / 4) is XORed with (row mod 8).
