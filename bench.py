@@ -460,6 +460,13 @@ def run_ours(args, rank, world, local):
         raise RuntimeError(f"device status 0x{int(status.item()):x} in the timed region")
 
     value = args.steps * job_flops / elapsed / 1e12
+    # launches per step: one split + the energy kernel issued in chunks of
+    # ~48 waves (same rule as tt_mp2_energy_presplit_i8)
+    nblk = (nvir + 127) // 128
+    ipp = nblk * (nblk + 1) // 2
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    per_launch = max(1, sms * 48 // ipp)
+    energy_launches = -(-(pe - pb) // per_launch)
 
     # sanity check: 8 pairs against the fp64 CUDA-core kernel
     e_chk, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(pb, min(pe, pb + 8)))
@@ -536,7 +543,8 @@ def run_ours(args, rank, world, local):
             torch.cuda.synchronize(dev)
             ts.append(a.elapsed_time(b) / 1e3)
         t_e2e = max_over_ranks(statistics.mean(ts), world, dev)
-        h2d = (Bh.numel() + eoh.numel() + evh.numel()) * 4 * world
+        h2d = sum(distributed.host_bytes_needed(nocc, nvir, naux, r, world) for r in range(world))
+        h2d += (eoh.numel() + evh.numel()) * 4 * world
         e2e = {"value": job_flops / t_e2e / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": 8 * world, "ms_per_step": t_e2e * 1e3,
                "api": "trntensor_b200.mp2_energy" if world == 1 else
@@ -589,7 +597,7 @@ def run_ours(args, rank, world, local):
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps * (1 + energy_launches),
             "clocks": clk,
             "ao2mo": ao,
         }

@@ -77,6 +77,14 @@ int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir
 int tt_split_i8(const float* x, signed char* q, float* scale, long long rows, int cols,
                 int cols_pad, void* stream);
 
+/* tt_split_i8 for rows [row_begin, row_begin + row_count) of a total_rows x
+ * cols matrix, written into the slice planes of the whole matrix (plane
+ * stride total_rows * cols_pad). Lets a caller split B as its rows arrive
+ * (e.g. while copying it from host memory in chunks). */
+int tt_split_i8_rows(const float* x, signed char* q, float* scale, long long row_begin,
+                     long long row_count, long long total_rows, int cols, int cols_pad,
+                     void* stream);
+
 /* tt_mp2_energy_f32 on operands already split by tt_split_i8 with rows =
  * nocc * nvir and cols_pad = naux_pad (lets callers reuse one split). */
 int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux_pad,

@@ -201,3 +201,26 @@ def test_paired_sm_kernel(cuda_ok, shape, monkeypatch):
     e1, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(1, npairs))
     e0, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(0, 1))
     assert rel(e0.item() + e1.item(), ref) <= RTOL_F32
+
+
+def test_host_pipelined_copy(cuda_ok):
+    """Pinned host B: copy overlapped with compute in row chunks (last rows
+    first); same energy as the device-resident path, also on pair ranges."""
+    from trntensor_b200.dispatch import first_row_of_pair, pair_offset
+
+    nocc = 37
+    for p in range(nocc * (nocc + 1) // 2):
+        i = first_row_of_pair(p, nocc)
+        assert pair_offset(i, nocc) <= p < pair_offset(i + 1, nocc)
+    B, eo, ev = mp2_inputs(nocc, 300, 130, seed=4)
+    Bp = B.pin_memory()
+    ref, _ = _cuda_mp2_energy(B.cuda(), eo, ev)
+    e, _ = _cuda_mp2_energy(Bp, eo, ev)
+    assert rel(e.item(), ref.item()) <= 1e-12
+    e_pub = tt.mp2_energy(Bp, eo, ev)
+    assert e_pub.device.type == "cpu" and rel(e_pub.item(), ref.item()) <= 1e-6
+    npairs = nocc * (nocc + 1) // 2
+    for rng in ((0, 100), (100, 550), (550, npairs), (5, 6)):
+        a, _ = _cuda_mp2_energy(Bp, eo, ev, pair_range=rng)
+        b, _ = _cuda_mp2_energy(B.cuda(), eo, ev, pair_range=rng)
+        assert abs(a.item() - b.item()) <= 1e-12 * abs(ref.item())

@@ -63,7 +63,8 @@ int split_operand(const float* X, const Operand& o, size_t mn, size_t K, int bat
     const long long cap = (long long)sms * 16;
     if (blocks > cap) blocks = cap;
     if (rows == 0) return TT_OK;
-    mp2::split_kernel<<<(unsigned)blocks, 256, 0, s>>>(X, Q, S, rows, (int)K, (int)o.inner);
+    mp2::split_kernel<<<(unsigned)blocks, 256, 0, s>>>(X, Q, S, rows, (int)K, (int)o.inner,
+                                                     rows * (long long)o.inner);
   } else {
     const long long nblk = (long long)batch * ((o.inner + oz::kSplitCols - 1) / oz::kSplitCols);
     const long long cap = (long long)sms * 8;

@@ -404,11 +404,13 @@ static __global__ void __launch_bounds__(kThreads, 1)
 // Every step is exact in fp32 (power-of-two scaling, Sterbenz subtraction).
 __device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
 
+// `plane` is the distance in bytes between the three slice planes (rows of
+// a larger matrix can be split piecewise into one set of planes).
 static __global__ void split_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
-                             float* __restrict__ scale, long long rows, int cols, int cols_pad) {
+                             float* __restrict__ scale, long long rows, int cols, int cols_pad,
+                             long long plane) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const long long plane = rows * (long long)cols_pad;
   for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
        r += warps) {
     const float* xr = x + r * cols;

@@ -131,6 +131,14 @@ def _cuda_mp2_energy(
     dev = _device()
     cdt = mp2_compute_dtype(B, precision)
     nocc, nvir, naux = (int(s) for s in B.shape)
+    if (
+        B.device.type == "cpu" and B.is_pinned() and B.dtype == torch.float32
+        and B.is_contiguous() and cdt == torch.float32 and kernel == "tc"
+        and not return_partials
+    ):
+        npairs = int(lib.tt_mp2_num_pairs(nocc))
+        pb, pe = (0, npairs) if pair_range is None else (int(pair_range[0]), int(pair_range[1]))
+        return _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe), None
     Bd = _to_dev(B, dev, cdt)
     eo = _to_dev(eps_occ, dev, cdt)
     ev = _to_dev(eps_vir, dev, cdt)
@@ -179,6 +187,87 @@ def _cuda_mp2_energy(
     _lib.check(st, "tt_mp2_energy_f32")
     _check_status(dev_status, "tt_mp2_energy_f32")
     return energy, partials
+
+
+def pair_offset(i: int, nocc: int) -> int:
+    """Linear id of the first unordered pair (i, i) (row-major over i <= j)."""
+    return i * nocc - i * (i - 1) // 2
+
+
+def first_row_of_pair(p: int, nocc: int) -> int:
+    """Occupied index i of the unordered pair with linear id p."""
+    lo, hi = 0, nocc - 1
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if pair_offset(mid, nocc) <= p:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
+def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
+    """fp32 DF-MP2 energy of host-resident pinned B with the copy overlapped.
+
+    Pairs (i, j), i <= j, with i >= a only need B rows a..nocc-1, and in
+    row-major pair order they form one contiguous id range. B is therefore
+    copied in row chunks from the last row backwards on a side stream; each
+    chunk is split into int8 slices as it lands (tt_split_i8_rows) and its
+    pair range is computed on the current stream while the next chunk is in
+    flight. Only the rows the pair range needs are copied.
+    """
+    nocc, nvir, naux = (int(s) for s in B.shape)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    eo = _to_dev(eps_occ, dev, torch.float32)
+    ev = _to_dev(eps_vir, dev, torch.float32)
+    if pe <= pb:
+        return torch.zeros((), dtype=torch.float64, device=dev)
+    pad = (naux + 63) // 64 * 64
+    rows_total = nocc * nvir
+    ws_bytes = int(lib.tt_mp2_workspace_bytes(nocc, nvir, naux))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    qbytes = (3 * rows_total * pad + 255) // 256 * 256
+    q_ptr = ws.data_ptr()
+    s_ptr = ws.data_ptr() + qbytes
+    Bd = torch.empty((nocc, nvir, naux), dtype=torch.float32, device=dev)
+    i0 = first_row_of_pair(pb, nocc)
+    step = max(1, -(-(nocc - i0) // chunks))
+    bounds = []
+    b = nocc
+    while b > i0:
+        a = max(i0, b - step)
+        bounds.append((a, b))
+        b = a
+    energies = torch.zeros(len(bounds), dtype=torch.float64, device=dev)
+    status = torch.zeros(len(bounds), dtype=torch.int32, device=dev)
+    copy_stream = torch.cuda.Stream(dev)
+    copy_stream.wait_stream(stream)  # Bd / ws allocations are ordered before the copies
+    for c, (a, b) in enumerate(bounds):
+        with torch.cuda.stream(copy_stream):
+            Bd[a:b].copy_(B[a:b], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(copy_stream)
+        stream.wait_event(done)
+        _lib.check(lib.tt_split_i8_rows(ctypes.c_void_p(Bd.data_ptr()), ctypes.c_void_p(q_ptr),
+                                        ctypes.c_void_p(s_ptr), a * nvir, (b - a) * nvir,
+                                        rows_total, naux, pad, sp), "tt_split_i8_rows")
+        lo = max(pb, pair_offset(a, nocc))
+        hi = min(pe, pair_offset(b, nocc) if b < nocc else nocc * (nocc + 1) // 2)
+        if hi > lo:
+            st = lib.tt_mp2_energy_presplit_i8(
+                ctypes.c_void_p(q_ptr), ctypes.c_void_p(s_ptr), pad, _ptr(eo), _ptr(ev), nocc,
+                nvir, lo, hi, ctypes.c_void_p(energies.data_ptr() + 8 * c), None,
+                ctypes.c_void_p(status.data_ptr() + 4 * c), sp)
+            _lib.check(st, "tt_mp2_energy_presplit_i8")
+    Bd.record_stream(copy_stream)
+    energy = energies.sum()
+    if os.environ.get("TRNTENSOR_B200_ASYNC", "") not in ("1", "true", "yes"):
+        bad = status.nonzero()
+        if bad.numel():
+            raise _lib.DeviceError(f"tt_mp2_energy_presplit_i8: device wait ran out "
+                                   f"(status 0x{int(status[bad[0, 0]].item()):x})")
+    return energy
 
 
 def _cuda_ao_to_mo_transform(

@@ -36,6 +36,16 @@ def aux_slab(naux: int, rank: int, world: int) -> tuple[int, int]:
     return pair_range(naux, rank, world)
 
 
+def host_bytes_needed(nocc: int, nvir: int, naux: int, rank: int, world: int) -> int:
+    """Bytes of a host fp32 B a rank copies: rows first_row(pair_begin)..nocc-1."""
+    from .dispatch import first_row_of_pair
+
+    pb, pe = pair_range(nocc * (nocc + 1) // 2, rank, world)
+    if pe <= pb:
+        return 0
+    return (nocc - first_row_of_pair(pb, nocc)) * nvir * naux * 4
+
+
 def reduce_energy(local: torch.Tensor, group=None) -> torch.Tensor:
     """Sum a 0-D fp64 tensor over the group (in place) and return it."""
     _, world = _world(group)
