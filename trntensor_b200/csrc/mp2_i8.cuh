@@ -349,25 +349,35 @@ static __global__ void __launch_bounds__(kThreads, 1)
           break;
         tc_fence_after();
         const float sa = arow ? __ldg(p.scale + (long long)t.j * p.nvir + a) : 0.f;
-        for (int c = c0; c < c0 + kBlk / 2; c += 16) {
+        // Combine all of this thread's y values into registers first so the
+        // accumulator goes back to the MMA warp before the energy is summed.
+        float y[kBlk / 2];
+#pragma unroll
+        for (int cc = 0; cc < kBlk / 32; ++cc) {
+          const int c = c0 + 16 * cc;
           int l2[16], l3[16], l4[16];
-          float x[16], y[16];
           tmem_ld16i(lane_base + 0 * kBlk + c, l2);
           tmem_ld16i(lane_base + 1 * kBlk + c, l3);
           tmem_ld16i(lane_base + 2 * kBlk + c, l4);
-          tmem_ld16(lane_base + kColStash + c, x);
           tmem_ld_wait();
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
             const int b = t.b0 + c + k;
             const float sb = b < p.nvir ? __ldg(p.scale + (long long)t.i * p.nvir + b) : 0.f;
-            y[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
+            y[16 * cc + k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
           }
-          acc += chunk_energy(c, x, y);
         }
         tc_fence_before();
         mbar_arrive(acc_empty);
         ++round;
+#pragma unroll
+        for (int cc = 0; cc < kBlk / 32; ++cc) {
+          const int c = c0 + 16 * cc;
+          float x[16];
+          tmem_ld16(lane_base + kColStash + c, x);
+          tmem_ld_wait();
+          acc += chunk_energy(c, x, *reinterpret_cast<const float(*)[16]>(y + 16 * cc));
+        }
       }
       const double wgt = (t.i == t.j) ? 1.0 : 2.0;
       my_energy += wgt * acc;
