@@ -73,7 +73,8 @@ int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir
 
 /* Ozaki split of x (rows x cols, row-major fp32): per row a power-of-two
  * scale[r] and three int8 slice planes q[t][r][0..cols_pad) (zero padded,
- * cols_pad % 64 == 0) with x = scale * (q1 + q2/2^7 + q3/2^14) + O(2^-22 max). */
+ * cols_pad % 64 == 0) with x = scale * (q1 + q2/2^8 + q3/2^16) + r, |r| <= scale/2^17,
+ * scale = 2^(e-6) with max|x| < 2^e (NaN for a row holding inf or NaN). */
 int tt_split_i8(const float* x, signed char* q, float* scale, long long rows, int cols,
                 int cols_pad, void* stream);
 

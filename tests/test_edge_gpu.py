@@ -89,3 +89,29 @@ def test_zero_rows_are_safe(cuda_ok):
     ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
     e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
     assert np.isfinite(e.item()) and rel(e.item(), ref) <= 2e-6
+
+
+@pytest.mark.parametrize("bad", [float("nan"), float("inf")])
+def test_nonfinite_input_propagates(cuda_ok, bad):
+    """A NaN or inf in B gives a non-finite energy, as fp32 arithmetic on the
+    input would (the row's Ozaki scale becomes NaN instead of the bad value
+    vanishing from the row maximum)."""
+    B, eo, ev = mp2_inputs(3, 150, 40, seed=2)
+    B[2, 31, 5] = bad
+    e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
+    assert not np.isfinite(e.item())
+
+
+def test_nonfinite_eri_propagates(cuda_ok):
+    """AO->MO: an inf in eri[m, n, P] makes B[:, :, P] non-finite, the other
+    aux columns stay finite and match the clean transform."""
+    from trntensor_b200.inputs import ao2mo_inputs
+
+    eri, co, cv = ao2mo_inputs(130, 5, 20, 70, seed=3)
+    clean = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda()).cpu()
+    eri[17, 40, 9] = float("inf")
+    out = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda()).cpu()
+    assert not torch.isfinite(out[:, :, 9]).all()
+    keep = torch.ones(70, dtype=torch.bool)
+    keep[9] = False
+    assert torch.equal(out[:, :, keep], clean[:, :, keep])

@@ -157,6 +157,7 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
   if (!eri || !C_occ || !C_vir || !workspace || !B_out || !dev_status) return TT_ERR_NULL;
   if (nbf <= 0 || nocc <= 0 || nvir <= 0 || naux <= 0) return TT_ERR_SHAPE;
   if ((long long)nbf * naux > 0x7fffffffLL) return TT_ERR_SHAPE;
+  if (nbf > ozd::kMaxK) return TT_ERR_SHAPE;  // int32 slice sums exact up to this K
   const OzLayout L(nbf, nocc, nvir, naux);
   if (workspace_bytes < L.total) return TT_ERR_WORKSPACE;
   if (!aligned16(workspace)) return TT_ERR_ALIGN;

@@ -105,6 +105,7 @@ int tt_gemm_f32(const float* A, int a_kmajor, long long strideA, const float* B,
   using namespace tt;
   if (!A || !B || !C || !workspace || !dev_status) return TT_ERR_NULL;
   if (M <= 0 || N <= 0 || K <= 0 || batch <= 0) return TT_ERR_SHAPE;
+  if (K > ozd::kMaxK) return TT_ERR_SHAPE;  // int32 slice sums exact up to this K
   const Operand oa(a_kmajor != 0, M, K, batch), ob(b_kmajor != 0, N, K, batch);
   if (workspace_bytes < oa.qbytes + oa.sbytes + ob.qbytes + ob.sbytes) return TT_ERR_WORKSPACE;
   if (!aligned16(workspace)) return TT_ERR_ALIGN;

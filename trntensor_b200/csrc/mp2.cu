@@ -158,7 +158,7 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
                               double* pair_partials, int* dev_status, void* stream) {
   if (!Q || !scale || !eps_occ || !eps_vir || !energy || !dev_status) return TT_ERR_NULL;
   if (nocc <= 0 || nvir <= 0 || naux_pad <= 0 || naux_pad % 64 != 0) return TT_ERR_SHAPE;
-  if (nocc > 65535 || nvir > 65535) return TT_ERR_SHAPE;
+  if (nocc > 65535 || nvir > 65535 || naux_pad > ozd::kMaxK) return TT_ERR_SHAPE;
   if (check_pairs(nocc, pair_begin, pair_end) != TT_OK) return TT_ERR_SHAPE;
   if (!aligned16(Q)) return TT_ERR_ALIGN;
   int dev = 0;

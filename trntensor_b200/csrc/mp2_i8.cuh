@@ -9,13 +9,13 @@
 // zero, so a K = 6144 contraction in 3xTF32 comes out biased by ~1e-4
 // (measured), far outside the 1e-6 energy tolerance. Integer MMAs
 // accumulate exactly. Each B row r = (i, a) is written as
-//     B[r, P] = s_r * (q1 + q2 / 2^7 + q3 / 2^14)[r, P] + O(s_r 2^-15),
+//     B[r, P] = s_r * (q1 + q2 / 2^8 + q3 / 2^16)[r, P] + O(s_r 2^-17),
 // s_r a power of two, q_t int8 ("slices", Ozaki et al. error-free
-// splitting with a per-row exponent), and
-//     T_ab = s_a s_b (L2 + L3 / 2^7 + L4 / 2^14),
+// splitting with a per-row exponent; format in ozaki_digits.cuh), and
+//     T_ab = s_a s_b (L2 + L3 / 2^8 + L4 / 2^16),
 //     L2 = Q1.Q1^T, L3 = Q1.Q2^T + Q2.Q1^T, L4 = Q1.Q3^T + Q2.Q2^T + Q3.Q1^T
 // are six exact int8 GEMMs accumulated in int32 TMEM columns (one column
-// block per level). Dropped terms are O(2^-21) relative and unbiased.
+// block per level). Dropped terms are O(2^-23) relative and unbiased.
 //
 // Work decomposition: unordered occupied pairs i <= j (E_ij == E_ji, weight
 // 2 for i < j), square 128 x 128 virtual blocks A <= B covering the upper
@@ -30,6 +30,7 @@
 // issuer, warps 2..9 = epilogue (lane quarter = warp % 4, column half =
 // (warp - 2) / 4).
 #pragma once
+#include "ozaki_digits.cuh"
 #include "ptx.cuh"
 
 namespace tt {
@@ -98,9 +99,7 @@ __device__ inline Item item_decode(long long w, const Params& p) {
   return it;
 }
 
-__device__ __forceinline__ float level_combine(int l2, int l3, int l4) {
-  return (float)l2 + (float)l3 * (1.0f / 128.0f) + (float)l4 * (1.0f / 16384.0f);
-}
+using ozd::level_combine;
 
 static __global__ void __launch_bounds__(kThreads, 1)
     energy_kernel(const __grid_constant__ CUtensorMap mapQ, Params p) {
@@ -261,7 +260,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
       const Item t = item_decode(w, p);
       const int a = t.a0 + row;
       const bool arow = a < p.nvir;
-      // ---- phase x: park s_ia s_jb (L2 + L3/2^7 + L4/2^14) in the stash columns
+      // ---- phase x: park s_ia s_jb (L2 + L3/2^8 + L4/2^16) in the stash columns
       if (!group_all<32 * kEpiWarps>(mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)))
         break;
       tc_fence_after();
@@ -409,11 +408,8 @@ static __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Ozaki split of one row per warp: s = 2^(e-7) with max|x| * 2^(7-e) <= 127,
-// q1 = rint(x/s), q2 = rint((x/s - q1) 2^7), q3 = rint(((x/s - q1) 2^7 - q2) 2^7).
-// Every step is exact in fp32 (power-of-two scaling, Sterbenz subtraction).
-__device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
-
+// Ozaki split of one row per warp into the slice format of ozaki_digits.cuh
+// (row scale s, three int8 slice planes).
 // `plane` is the distance in bytes between the three slice planes (rows of
 // a larger matrix can be split piecewise into one set of planes).
 static __global__ void split_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
@@ -425,35 +421,22 @@ static __global__ void split_kernel(const float* __restrict__ x, int8_t* __restr
        r += warps) {
     const float* xr = x + r * cols;
     float m = 0.f;
-    for (int c = lane; c < cols; c += 32) m = fmaxf(m, fabsf(__ldg(xr + c)));
+    for (int c = lane; c < cols; c += 32) m = ozd::absmax(m, __ldg(xr + c));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    int e = 0;
-    float inv = 0.f, s = 0.f;
-    if (m > 0.f && m < 3.0e38f && m > 1.0e-30f) {
-      e = ilogbf(m) + 1;  // m < 2^e
-      if (m * pow2f(7 - e) > 127.f) ++e;
-      inv = pow2f(7 - e);
-      s = pow2f(e - 7);
-    }
+    const float s = ozd::scale_for_max(m);
+    const float inv1 = ozd::inv_scale(s);
     if (lane == 0) scale[r] = s;
     int8_t* q1 = q + r * cols_pad;
     int8_t* q2 = q1 + plane;
     int8_t* q3 = q2 + plane;
+    const float inv[4] = {inv1, inv1, inv1, inv1};
     for (int c = lane * 4; c < cols_pad; c += 128) {
-      uint32_t w1 = 0, w2 = 0, w3 = 0;
+      float v[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float v = (c + k < cols) ? __ldg(xr + c + k) * inv : 0.f;
-        const float d1 = rintf(v);
-        const float r1 = (v - d1) * 128.f;
-        const float d2 = rintf(r1);
-        const float r2 = (r1 - d2) * 128.f;
-        const float d3 = rintf(r2);
-        w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * k);
-        w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * k);
-        w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * k);
-      }
+      for (int k = 0; k < 4; ++k) v[k] = (c + k < cols) ? __ldg(xr + c + k) : 0.f;
+      uint32_t w1, w2, w3;
+      ozd::split4(v, inv, w1, w2, w3);
       *reinterpret_cast<uint32_t*>(q1 + c) = w1;
       *reinterpret_cast<uint32_t*>(q2 + c) = w2;
       *reinterpret_cast<uint32_t*>(q3 + c) = w3;

@@ -2,14 +2,16 @@
 // "K rows, M/N contiguous" (MN-major), batched:
 //   C[b][m][n] = sum_k A[bA][k][m] B[b][k][n]
 // Each operand column (fixed m or n, all k) gets a power-of-two scale s and
-// three int8 slices: X[k][c] = s_c (q1 + q2/2^7 + q3/2^14)[k][c] + O(2^-22).
-// Then C = sA_m sB_n (L2 + L3/2^7 + L4/2^14) with six exact int8 GEMMs
+// three int8 slices: X[k][c] = s_c (q1 + q2/2^8 + q3/2^16)[k][c] + O(s_c 2^-17)
+// (format in ozaki_digits.cuh).
+// Then C = sA_m sB_n (L2 + L3/2^8 + L4/2^16) with six exact int8 GEMMs
 // accumulated in int32 TMEM (see csrc/mp2_i8.cuh for the same scheme on
 // K-major rows). Used for both steps of the AO->MO transform.
 //
 // Tile: M = N = 128 (one 128-byte SW128 atom wide in M/N), 64 k per stage.
 // Roles: warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue.
 #pragma once
+#include "ozaki_digits.cuh"
 #include "ptx.cuh"
 
 namespace tt {
@@ -39,9 +41,7 @@ struct Params {
   int* err;
 };
 
-__device__ __forceinline__ float level_combine(int l2, int l3, int l4) {
-  return (float)l2 + (float)l3 * (1.0f / 128.0f) + (float)l4 * (1.0f / 16384.0f);
-}
+using ozd::level_combine;
 
 struct Tile {
   int b, m0, n0;
@@ -235,26 +235,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Column-scaled Ozaki split of X[b][k][n] (row stride ldx, batch stride bsx):
-// S[b][n] = 2^(e-7) with max_k |X[b][k][n]| 2^(7-e) <= 127; Q[t][b][k][n]
-// (row length npad, zero padding) the three int8 slices. One block handles 32
-// columns of one batch for all k.
-__device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
-
 // Column-scaled split in two streaming passes over X[b][k][n]:
 //   colmax_kernel: S[b][n] = power-of-two scale of column n (max over k);
-//   slice_kernel : Q[t][b][k][n] int8 slices with that scale.
+//   slice_kernel : Q[t][b][k][n] int8 slices with that scale (row length
+//                  npad, zero padding; row stride ldx, batch stride bsx).
 // A block covers 128 columns (4 per lane, 16-byte accesses when the row
 // stride allows) and all k; its 8 warps take every 8th row.
 constexpr int kSplitThreads = 256;
 constexpr int kSplitCols = 128;
 
-__device__ __forceinline__ float scale_for_max(float mx) {
-  if (!(mx > 1.0e-30f && mx < 3.0e38f)) return 0.f;
-  int e = ilogbf(mx) + 1;
-  if (mx * pow2f(7 - e) > 127.f) ++e;
-  return pow2f(e - 7);
-}
+using ozd::scale_for_max;
 
 __device__ __forceinline__ void load4(const float* xc, bool vec, int nvalid, float (&v)[4]) {
   if (vec && nvalid >= 4) {
@@ -285,7 +275,7 @@ static __global__ void __launch_bounds__(kSplitThreads)
         float v[4];
         load4(xc + (long long)k * ldx, vec, nvalid, v);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) mx[j] = fmaxf(mx[j], fabsf(v[j]));
+        for (int j = 0; j < 4; ++j) mx[j] = ozd::absmax(mx[j], v[j]);
       }
     }
 #pragma unroll
@@ -302,21 +292,6 @@ static __global__ void __launch_bounds__(kSplitThreads)
   }
 }
 
-__device__ __forceinline__ void slice4(const float (&v)[4], const float (&inv)[4], uint32_t& w1,
-                                       uint32_t& w2, uint32_t& w3) {
-  w1 = w2 = w3 = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float x = v[j] * inv[j];
-    const float d1 = rintf(x);
-    const float r1 = (x - d1) * 128.f;
-    const float d2 = rintf(r1);
-    const float d3 = rintf((r1 - d2) * 128.f);
-    w1 |= ((uint32_t)(int)d1 & 0xffu) << (8 * j);
-    w2 |= ((uint32_t)(int)d2 & 0xffu) << (8 * j);
-    w3 |= ((uint32_t)(int)d3 & 0xffu) << (8 * j);
-  }
-}
 
 // Loads of kSliceRows rows are issued before any arithmetic so that each
 // thread keeps several 16-byte reads in flight.
@@ -340,7 +315,7 @@ static __global__ void __launch_bounds__(kSplitThreads, 3)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float sc = S[(long long)b * npad + n + j];
-      inv[j] = sc > 0.f ? 1.0f / sc : 0.f;  // exact: sc is a power of two
+      inv[j] = ozd::inv_scale(sc);
     }
     int8_t* q1 = Q + (long long)b * K * npad + n;
     for (int k0 = wp; k0 < K; k0 += kWarps * kSliceRows) {
@@ -356,7 +331,7 @@ static __global__ void __launch_bounds__(kSplitThreads, 3)
         const int k = k0 + r * kWarps;
         if (k >= K) break;
         uint32_t w1, w2, w3;
-        slice4(v[r], inv, w1, w2, w3);
+        ozd::split4(v[r], inv, w1, w2, w3);
         const long long o = (long long)k * npad;
         *reinterpret_cast<uint32_t*>(q1 + o) = w1;
         *reinterpret_cast<uint32_t*>(q1 + o + plane) = w2;

@@ -257,7 +257,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 4; ++k) {
         const int n = n0 + 4 * lane + k;
         const float sc = n < p.N ? __ldg(p.sX + n) : 0.f;
-        inv[k] = sc > 0.f ? 16384.0f / sc : 0.f;  // exact: sc is a power of two
+        inv[k] = ozd::inv_scale(sc);
       }
       for (int kc = 0; kc < nkc; ++kc, ++it) {
         const int f = it % kFStages, s = it % kIStages;
@@ -279,23 +279,10 @@ static __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < kRows; ++j) {
           const int r = cw + kCvtWarps * j;
-          // Y = round(x / s * 2^14) is exact in int32 (|Y| <= 127 * 2^14);
-          // its balanced base-128 digits are the slices:
-          //   q3 = ((Y + 64) & 127) - 64, Y' = (Y - q3) / 128, q2 likewise,
-          //   q1 = (Y' - q2) / 128, so x / s = q1 + q2 / 2^7 + q3 / 2^14 + O(2^-15).
-          const int Y[4] = {__float2int_rn(v[j].x * inv[0]), __float2int_rn(v[j].y * inv[1]),
-                            __float2int_rn(v[j].z * inv[2]), __float2int_rn(v[j].w * inv[3])};
-          uint32_t w1 = 0, w2 = 0, w3 = 0;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int d3 = ((Y[k] + 64) & 127) - 64;
-            const int y1 = (Y[k] - d3) >> 7;
-            const int d2 = ((y1 + 64) & 127) - 64;
-            const int d1 = (y1 - d2) >> 7;
-            w1 |= ((uint32_t)d1 & 0xffu) << (8 * k);
-            w2 |= ((uint32_t)d2 & 0xffu) << (8 * k);
-            w3 |= ((uint32_t)d3 & 0xffu) << (8 * k);
-          }
+          // slices of x / s (ozaki_digits.cuh): one FMA per value, byte permutes
+          const float x4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+          uint32_t w1, w2, w3;
+          ozd::split4(x4, inv, w1, w2, w3);
           // MN-major SW128 atom: 8 k-rows x 128 bytes; the 16-byte chunk
           // index (lane / 4) is XORed with (row mod 8).
           const int off = (r >> 3) * 1024 + (r & 7) * 128 + ((((lane >> 2) ^ (r & 7))) << 4) +

@@ -131,6 +131,8 @@ def _cuda_mp2_energy(
     dev = _device()
     cdt = mp2_compute_dtype(B, precision)
     nocc, nvir, naux = (int(s) for s in B.shape)
+    if kernel == "tc" and naux > OZAKI_MAX_K:
+        kernel = "simt"  # int32 slice sums are exact only up to OZAKI_MAX_K terms
     if (
         B.device.type == "cpu" and B.is_pinned() and B.dtype == torch.float32
         and B.is_contiguous() and cdt == torch.float32 and kernel == "tc"
@@ -187,6 +189,11 @@ def _cuda_mp2_energy(
     _lib.check(st, "tt_mp2_energy_f32")
     _check_status(dev_status, "tt_mp2_energy_f32")
     return energy, partials
+
+
+# Longest contraction the int8 Ozaki kernels sum exactly in int32
+# (csrc/ozaki_digits.cuh): K * (64*128 + 128*128 + 128*64) < 2^31.
+OZAKI_MAX_K = 65535
 
 
 def pair_offset(i: int, nocc: int) -> int:
@@ -291,9 +298,11 @@ def _cuda_ao_to_mo_transform(
     cdt = torch.float64 if (precision == "kahan" or eri.dtype == torch.float64) else torch.float32
     nbf, _, naux = (int(s) for s in eri.shape)
     nocc, nvir = int(C_occ.shape[1]), int(C_vir.shape[1])
-    out = torch.zeros((nocc, nvir, naux), dtype=cdt, device=dev)
-    if out.numel() == 0 or nbf == 0:
-        return out
+    if nocc * nvir * naux == 0 or nbf == 0:
+        return torch.zeros((nocc, nvir, naux), dtype=cdt, device=dev)
+    out = torch.empty((nocc, nvir, naux), dtype=cdt, device=dev)  # every element is written
+    if kernel == "tc" and nbf > OZAKI_MAX_K:
+        kernel = "simt"
     e = _to_dev(eri, dev, cdt)
     co = _to_dev(C_occ, dev, cdt)
     cv = _to_dev(C_vir, dev, cdt)

@@ -129,8 +129,12 @@ def _execute(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.T
 
 def _tensor_core_ok(plan: ContractionPlan, *ops: torch.Tensor) -> bool:
     """matmul/bmm plans on CUDA fp32 operands run on the int8 tensor-core GEMM."""
-    return plan.backend == "cuda" and all(
-        op.device.type == "cuda" and op.dtype == torch.float32 for op in ops
+    from .dispatch import OZAKI_MAX_K
+
+    return (
+        plan.backend == "cuda"
+        and all(op.device.type == "cuda" and op.dtype == torch.float32 for op in ops)
+        and ops[0].shape[-1] <= OZAKI_MAX_K
     )
 
 
