@@ -37,8 +37,8 @@ struct OzLayout {
   OzLayout(size_t nbf, size_t nocc, size_t nvir, size_t naux) {
     size_t o = 0;
     auto take = [&o](size_t bytes) { size_t r = o; o += al256(bytes); return r; };
-    qo = take(3 * nbf * pad16(nocc));
-    so = take(4 * pad16(nocc));
+    qo = take(3 * nbf * pad16(nocc) * ozc::kARep);  // replicated for the on-chip path
+    so = take(4 * pad16(nocc) * ozc::kARep);
     qv = take(3 * nbf * pad16(nvir));
     sv = take(4 * pad16(nvir));
     qe = take(3 * nbf * pad16(nbf * naux));
@@ -141,6 +141,10 @@ int ao2mo_simt(const T* eri, const T* C_occ, const T* C_vir, int nbf, int nocc, 
 }  // namespace
 }  // namespace tt
 
+// Debug hook: per-CTA wait-cycle counters of TT_OZC_PROFILE builds.
+static long long* g_ozc_prof = nullptr;
+extern "C" void tt_debug_set_ao2mo_profile_buffer(long long* buf) { g_ozc_prof = buf; }
+
 extern "C" {
 
 size_t tt_ao2mo_workspace_bytes(int nbf, int nocc, int nvir, int naux, int elem_bytes) {
@@ -181,12 +185,16 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
   const int sms = g_sms[dev];
   const int po = (int)pad16(nocc), pv = (int)pad16(nvir), pe = (int)pad16((size_t)nbf * naux),
             pa = (int)pad16(naux);
-  // Column-scaled int8 slices of the three operands of step 1 and of C_vir.
-  if ((st = split_cols(C_occ, nocc, 0, 1, nbf, nocc, po, qo, so, s, sms))) return st;
-  if ((st = split_cols(C_vir, nvir, 0, 1, nbf, nvir, pv, qv, sv, s, sms))) return st;
   const long long ncol = (long long)nbf * naux;
   const char* pre = std::getenv("TRNTENSOR_B200_AO2MO_PRESLICE");
   const bool preslice = (pre != nullptr && pre[0] == '1') || (ncol % 4 != 0) || !aligned16(eri);
+  // Column-scaled int8 slices of C_occ and C_vir. For the on-chip path C_occ's
+  // slices are written kARep times (batch stride 0 on the source): every CTA
+  // re-reads them for each tile, and spreading those reads over several copies
+  // keeps them off a few hot L2 lines.
+  if ((st = split_cols(C_occ, nocc, 0, preslice ? 1 : ozc::kARep, nbf, nocc, po, qo, so, s, sms)))
+    return st;
+  if ((st = split_cols(C_vir, nvir, 0, 1, nbf, nvir, pv, qv, sv, s, sms))) return st;
   if (preslice) {
     // eri split into int8 slices in HBM, then the generic slice GEMM
     if ((st = split_cols(eri, ncol, 0, 1, nbf, nbf * naux, pe, qe, se, s, sms))) return st;
@@ -204,7 +212,7 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     const uint64_t xd[2] = {(uint64_t)ncol, (uint64_t)nbf};
     const uint64_t xs[1] = {(uint64_t)ncol * 4};
     const uint32_t xb[2] = {(uint32_t)ozc::kTile, (uint32_t)ozc::kKC};
-    if (slice_map(&ma, qo, po, nbf, 1) ||
+    if (slice_map(&ma, qo, po, nbf, ozc::kARep) ||
         encode_tmap(&mx, eri, 2, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_NONE))
       return TT_ERR_TMA;
     ozc::Params pc;
@@ -218,6 +226,7 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     pc.tiles_m = (nocc + ozc::kTile - 1) / ozc::kTile;
     pc.tiles_n = (int)((ncol + ozc::kTile - 1) / ozc::kTile);
     pc.err = dev_status;
+    pc.prof = g_ozc_prof;
     const long long tiles = (long long)pc.tiles_m * pc.tiles_n;
     const int grid = (int)(tiles < sms ? tiles : sms);
     ozc::gemm_cvt_kernel<<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);

@@ -1,21 +1,30 @@
 // Step 1 of the AO->MO transform with the B operand converted on chip:
 //   C[m][n] = sum_k A[k][m] X[k][n]
-// A: int8 Ozaki slices of C_occ (MN-major, as in ozaki_gemm.cuh);
+// A: int8 Ozaki slices of C_occ (MN-major, as in ozaki_gemm.cuh), kARep
+//    identical copies;
 // X: fp32 rows (eri viewed as nbf x nbf*naux), read once by TMA in
 //    64 x 128 tiles and split in shared memory, with the column scales s_n
 //    (max over all k) computed beforehand by colmax_kernel.
 // This removes the separate slice pass and its 3 bytes/element round trip
 // through HBM. Two rings in shared memory:
-//   fp32 landing ring (3 x 32 KB): one producer lane's TMA fills X tiles;
+//   fp32 landing ring (3 x 32 KB): one producer warp's TMA fills X tiles;
 //     converter warps read their rows (lane l: one float4 of a row, a warp
 //     reads a whole row) and release the slot at once, so the ring only has
 //     to cover HBM latency;
-//   int8 ring (2 x 48 KB): a second producer lane's TMA brings the A slice
+//   int8 ring (2 x 48 KB): a second producer warp's TMA brings the A slice
 //     tiles; converter warps write the three B slice tiles in the MN-major
 //     128B-swizzled layout the MMA descriptors expect (one 32-bit store per
 //     lane and slice, a warp writes a whole 128-byte row), fence the async
 //     proxy and arrive on conv; the MMA thread waits on fullA and conv.
-// Roles: warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue, 10..17 convert.
+//     The A loads have their own warp so that they run ahead of the MMA
+//     independently of the fp32 stream.
+// Epilogue: the three level accumulators (TMEM columns 0..383) are combined
+// into fp32 and parked in columns 384..511, which releases the accumulator
+// to the next tile's MMAs at once; the parked tile then leaves through a
+// 16-column shared-memory stage as coalesced row segments.
+// Roles: warp 0 fp32 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue, 10..17
+// convert, warp 18 A-slice TMA (a separate warp, so that neither producer's
+// barrier wait holds up the other).
 #pragma once
 #include "ozaki_gemm.cuh"
 
@@ -26,6 +35,8 @@ using oz::kTile;  // 128
 using oz::kKC;    // 64
 using oz::level_combine;
 
+// Ring depths: a 2-deep fp32 ring (with a 3-deep int8 ring) gave intermittently
+// wrong 32-byte column groups in the output and was not used; 3 + 2 is exact.
 constexpr int kFStages = 3;                   // fp32 landing ring (TMA -> converters)
 constexpr int kIStages = 2;                   // int8 ring (A by TMA, B by converters -> MMA)
 constexpr int kFBytes = kTile * kKC * 4;      // 32 KB fp32 tile
@@ -33,11 +44,14 @@ constexpr int kARegion = 3 * kTile * kKC;     // 24 KB of A slices
 constexpr int kIBytes = 2 * kARegion;         // A and B slices: 48 KB
 constexpr int kEpiWarps = 8;
 constexpr int kCvtWarps = 8;   // (16 converter + 4 epilogue warps measured no faster)
-constexpr int kThreads = 64 + 32 * (kEpiWarps + kCvtWarps);
-constexpr int kQCols = kTile / 4;             // output staged a quarter tile at a time
+constexpr int kAWarp = 2 + kEpiWarps + kCvtWarps;  // A-slice producer (its own warp)
+constexpr int kThreads = 32 * (kAWarp + 1);
+constexpr int kQCols = 16;                    // output staged 16 columns at a time
 constexpr int kQLd = kQCols + 4;
+constexpr int kColPark = 3 * kTile;           // TMEM columns of the parked fp32 tile
+constexpr int kARep = 8;                      // copies of the A slices (CTA b reads copy b % kARep)
 constexpr int kOutBytes = kTile * kQLd * 4;
-constexpr int kSmemBytes = kFStages * kFBytes + kIStages * kIBytes + kOutBytes + 1024 + 256;
+constexpr int kSmemBytes = kFStages * kFBytes + kIStages * kIBytes + kOutBytes + kTile * 4 + 1024 + 256;
 
 struct Params {
   const float* sA;    // column scales of A (per m)
@@ -47,6 +61,7 @@ struct Params {
   int M, N, K;
   int tiles_m, tiles_n;
   int* err;
+  long long* prof;  // optional per-CTA wait-cycle counters (TT_OZC_PROFILE builds)
 };
 
 static __global__ void __launch_bounds__(kThreads, 1)
@@ -57,7 +72,8 @@ static __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* fring = smem;
   uint8_t* iring = smem + kFStages * kFBytes;
   float* ostage = (float*)(iring + kIStages * kIBytes);
-  uint64_t* fullF = (uint64_t*)((uint8_t*)ostage + kOutBytes);
+  float* escale = (float*)((uint8_t*)ostage + kOutBytes);  // column scales of the tile
+  uint64_t* fullF = (uint64_t*)(escale + kTile);
   uint64_t* freeF = fullF + kFStages;
   uint64_t* fullA = freeF + kFStages;
   uint64_t* conv = fullA + kIStages;
@@ -78,7 +94,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kIStages; ++s) {
       mbar_init(&fullA[s], 1);
-      mbar_init(&conv[s], kCvtWarps);
+      mbar_init(&conv[s], 32 * kCvtWarps);
       mbar_init(&emptyI[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -102,12 +118,12 @@ static __global__ void __launch_bounds__(kThreads, 1)
     m0 = (int)(w % p.tiles_m) * kTile;
   };
 
-  if (warp == 0) {
-    // ----------------------------------------- producers (two lanes of warp 0)
-    // lane 0: fp32 X tiles into the landing ring; lane 16: A slice tiles into
-    // the int8 ring as soon as the MMA has released a slot.
-    if (lane == 0 || lane == 16) {
-      const bool fp32 = lane == 0;
+  if (warp == 0 || warp == kAWarp) {
+    // ------------------------------------------------ producers (one lane each)
+    // warp 0: fp32 X tiles into the landing ring; warp kAWarp: A slice tiles
+    // into the int8 ring as soon as the MMA has released a slot.
+    if (lane == 0) {
+      const bool fp32 = warp == 0;
       const int nst = fp32 ? kFStages : kIStages;
       uint64_t* wait_bar = fp32 ? freeF : emptyI;
       uint64_t* fill_bar = fp32 ? fullF : fullA;
@@ -127,7 +143,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(fring + s * kFBytes, &mapX, &fill_bar[s], n0, kc * kKC);
           } else {
             mbar_arrive_expect_tx(&fill_bar[s], kARegion);
-            tma_load_4d(iring + s * kIBytes, &mapA, &fill_bar[s], m0, kc * kKC, 0, 0);
+            tma_load_4d(iring + s * kIBytes, &mapA, &fill_bar[s], m0, kc * kKC, blockIdx.x % kARep, 0);
           }
         }
       }
@@ -141,17 +157,40 @@ static __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_s8(kTile, kTile, 1, 1);
       uint32_t it = 0, round = 0;
       bool ok = true;
+#ifdef TT_OZC_PROFILE
+      long long w_acc = 0, w_a = 0, w_c = 0;
+      const long long t_begin = clock64();
+#endif
       for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x, ++round) {
+#ifdef TT_OZC_PROFILE
+        long long t0 = clock64();
+#endif
         if (!mbar_wait(acc_empty, (round & 1u) ^ 1u, p.err, kDevTimeoutAccFree)) break;
+#ifdef TT_OZC_PROFILE
+        w_acc += clock64() - t0;
+#endif
         tc_fence_after();
         for (int kc = 0; kc < nkc; ++kc, ++it) {
           const int s = it % kIStages;
           const uint32_t ph = (it / kIStages) & 1u;
-          if (!mbar_wait(&fullA[s], ph, p.err, kDevTimeoutFull) ||
-              !mbar_wait(&conv[s], ph, p.err, kDevTimeoutFull)) {
+#ifdef TT_OZC_PROFILE
+          long long t1 = clock64();
+#endif
+          if (!mbar_wait(&fullA[s], ph, p.err, kDevTimeoutFull)) {
             ok = false;
             break;
           }
+#ifdef TT_OZC_PROFILE
+          long long t2 = clock64();
+          w_a += t2 - t1;
+#endif
+          if (!mbar_wait(&conv[s], ph, p.err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+#ifdef TT_OZC_PROFILE
+          w_c += clock64() - t2;
+#endif
           tc_fence_after();
           const uint32_t sa = smem_u32(iring + s * kIBytes);
           const uint32_t sb = sa + kARegion;
@@ -177,6 +216,14 @@ static __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(final_bar);
       mbar_wait_drain(final_bar, 0);
+#ifdef TT_OZC_PROFILE
+      if (p.prof) {
+        p.prof[blockIdx.x * 8 + 0] = clock64() - t_begin;
+        p.prof[blockIdx.x * 8 + 1] = w_acc;
+        p.prof[blockIdx.x * 8 + 2] = w_a;
+        p.prof[blockIdx.x * 8 + 3] = w_c;
+      }
+#endif
     }
   } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ epilogue
@@ -188,67 +235,75 @@ static __global__ void __launch_bounds__(kThreads, 1)
     const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
     uint32_t round = 0;
     for (long long w = blockIdx.x; w < n_tiles; w += gridDim.x, ++round) {
+      int m0, n0;
+      tile_of(w, m0, n0);
+      // stage the tile's column scales while the MMAs run
+      if (ew < 4) {
+        const int n = n0 + ew * 32 + lane;
+        escale[ew * 32 + lane] = n < p.N ? __ldg(p.sX + n) : 0.f;
+      }
       if (!group_all<32 * kEpiWarps, 1>(mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)))
         break;
       tc_fence_after();
-      int m0, n0;
-      tile_of(w, m0, n0);
       const int m = m0 + row;
       const float sa = m < p.M ? __ldg(p.sA + m) : 0.f;
       const int nn = p.N - n0 < kTile ? p.N - n0 : kTile;
-      // Four rounds through a quarter-tile stage: the warps owning columns
-      // [32h, 32h+32) drain them, then all eight warps store 128 rows x 32
-      // columns with coalesced row segments.
-      for (int h = 0; h < 4; ++h) {
-        if (half == (h >> 1)) {
+      // combine this thread's 64 columns and park them as fp32
 #pragma unroll
-          for (int c = 0; c < kQCols; c += 16) {
-            const int cc = h * kQCols + c;
-            int l2[16], l3[16], l4[16];
-            tmem_ld16i(lane_base + 0 * kTile + cc, l2);
-            tmem_ld16i(lane_base + 1 * kTile + cc, l3);
-            tmem_ld16i(lane_base + 2 * kTile + cc, l4);
-            tmem_ld_wait();
-            float v[16];
+      for (int c = half * (kTile / 2); c < (half + 1) * (kTile / 2); c += 16) {
+        int l2[16], l3[16], l4[16];
+        tmem_ld16i(lane_base + 0 * kTile + c, l2);
+        tmem_ld16i(lane_base + 1 * kTile + c, l3);
+        tmem_ld16i(lane_base + 2 * kTile + c, l4);
+        tmem_ld_wait();
+        float v[16];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              const int n = n0 + cc + k;
-              const float sb = n < p.N ? __ldg(p.sX + n) : 0.f;
-              v[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * sb);
-            }
-            float4* dst = reinterpret_cast<float4*>(ostage + row * kQLd + c);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-          }
-        }
-        tc_fence_before();
-        if (h == 3) mbar_arrive(acc_empty);  // all columns drained: TMEM is free
-        group_sync<32 * kEpiWarps, 1>();
+        for (int k = 0; k < 16; ++k) v[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * escale[c + k]);
+        tmem_st16(lane_base + kColPark + c, v);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(acc_empty);  // levels drained: the next tile's MMAs may start
+      // Eight rounds through the 16-column stage: the warps owning columns
+      // [16h, 16h+16) copy them out of TMEM, then all eight warps store
+      // 128 rows x 16 columns (4 lanes x float4 per row).
+      for (int h = 0; h < kTile / kQCols; ++h) {
         const int c0 = h * kQCols;
+        if (half == c0 / (kTile / 2)) {
+          float v[16];
+          tmem_ld16(lane_base + kColPark + c0, v);
+          tmem_ld_wait();
+          float4* dst = reinterpret_cast<float4*>(ostage + row * kQLd);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        }
+        group_sync<32 * kEpiWarps, 1>();
         const int ncols = nn - c0;
-        // 4 rows per warp instruction: 8 lanes x float4 = one 32-column row
-        for (int r = ew * 4 + (lane >> 3); r < kTile; r += 4 * kEpiWarps) {
+        const int l4 = lane & 3;
+        for (int r = ew * 8 + (lane >> 2); r < kTile; r += 8 * kEpiWarps) {
           const int mm = m0 + r;
           if (mm >= p.M || ncols <= 0) continue;
           float* crow = p.C + (long long)mm * p.ldc + n0 + c0;
           const float* srow = ostage + r * kQLd;
-          const int l8 = lane & 7;
           if (vec && ncols >= kQCols) {
-            reinterpret_cast<float4*>(crow)[l8] = reinterpret_cast<const float4*>(srow)[l8];
+            reinterpret_cast<float4*>(crow)[l4] = reinterpret_cast<const float4*>(srow)[l4];
           } else {
-            for (int c = l8; c < ncols && c < kQCols; c += 8) crow[c] = srow[c];
+            for (int c = l4; c < ncols && c < kQCols; c += 4) crow[c] = srow[c];
           }
         }
-        group_sync<32 * kEpiWarps, 1>();  // stage free for the next quarter
+        group_sync<32 * kEpiWarps, 1>();  // stage free for the next round
       }
     }
-  } else {
+  } else if (warp < kAWarp) {
     // ----------------------------------------------------------- converters
     const int cw = warp - (2 + kEpiWarps);
     constexpr int kRows = kKC / kCvtWarps;  // 8 rows per warp and stage
     uint32_t it = 0;
     bool ok = true;
+#ifdef TT_OZC_PROFILE
+    long long w_f = 0, w_e = 0;
+#endif
     for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
       int m0, n0;
       tile_of(w, m0, n0);
@@ -261,41 +316,64 @@ static __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int kc = 0; kc < nkc; ++kc, ++it) {
         const int f = it % kFStages, s = it % kIStages;
+#ifdef TT_OZC_PROFILE
+        long long t0 = clock64();
+#endif
         if (!mbar_wait(&fullF[f], (it / kFStages) & 1u, p.err, kDevTimeoutFull)) {
           ok = false;
           break;
         }
+#ifdef TT_OZC_PROFILE
+        long long t1 = clock64();
+        w_f += t1 - t0;
+#endif
         const float4* src = reinterpret_cast<const float4*>(fring + f * kFBytes);
-        float4 v[kRows];
+        // Split this warp's rows into registers first: the byte permutes
+        // consume every loaded value, so once all lanes are past them (the
+        // __syncwarp) no read of the slot is outstanding and it can be refilled.
+        uint32_t q[kRows][3];
 #pragma unroll
-        for (int j = 0; j < kRows; ++j) v[j] = src[(cw + kCvtWarps * j) * (kTile / 4) + lane];
+        for (int j = 0; j < kRows; ++j) {
+          const float4 v = src[(cw + kCvtWarps * j) * (kTile / 4) + lane];
+          const float x4[4] = {v.x, v.y, v.z, v.w};
+          ozd::split4(x4, inv, q[j][0], q[j][1], q[j][2]);  // one FMA per value
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&freeF[f]);  // this warp's rows are read
+        if (lane == 0) mbar_arrive(&freeF[f]);  // this warp's rows are consumed
+#ifdef TT_OZC_PROFILE
+        long long t2 = clock64();
+#endif
         if (!mbar_wait(&emptyI[s], ((it / kIStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
           ok = false;
           break;
         }
+#ifdef TT_OZC_PROFILE
+        w_e += clock64() - t2;
+#endif
         uint8_t* tile = iring + s * kIBytes + kARegion;
 #pragma unroll
         for (int j = 0; j < kRows; ++j) {
           const int r = cw + kCvtWarps * j;
-          // slices of x / s (ozaki_digits.cuh): one FMA per value, byte permutes
-          const float x4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-          uint32_t w1, w2, w3;
-          ozd::split4(x4, inv, w1, w2, w3);
           // MN-major SW128 atom: 8 k-rows x 128 bytes; the 16-byte chunk
           // index (lane / 4) is XORed with (row mod 8).
           const int off = (r >> 3) * 1024 + (r & 7) * 128 + ((((lane >> 2) ^ (r & 7))) << 4) +
                           (lane & 3) * 4;
-          *reinterpret_cast<uint32_t*>(tile + 0 * oz::kSliceTile + off) = w1;
-          *reinterpret_cast<uint32_t*>(tile + 1 * oz::kSliceTile + off) = w2;
-          *reinterpret_cast<uint32_t*>(tile + 2 * oz::kSliceTile + off) = w3;
+          *reinterpret_cast<uint32_t*>(tile + 0 * oz::kSliceTile + off) = q[j][0];
+          *reinterpret_cast<uint32_t*>(tile + 1 * oz::kSliceTile + off) = q[j][1];
+          *reinterpret_cast<uint32_t*>(tile + 2 * oz::kSliceTile + off) = q[j][2];
         }
+        // each thread makes its own slice writes visible to the tensor cores
+        // and arrives (conv counts every converter thread)
         fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[s]);
+        mbar_arrive(&conv[s]);
       }
     }
+#ifdef TT_OZC_PROFILE
+    if (p.prof && cw == 0 && lane == 0) {
+      p.prof[blockIdx.x * 8 + 4] = w_f;
+      p.prof[blockIdx.x * 8 + 5] = w_e;
+    }
+#endif
   }
 
   tc_fence_before();
