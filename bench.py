@@ -290,8 +290,10 @@ def run_reference(args, rank, world):
 
 
 # ------------------------------------------------------------- our arm
-def measure_int8_peak(device) -> float | None:
-    """Dense int8 GEMM TOPS via torch._int_mm (cuBLASLt), best of 10."""
+def measure_int8_peak(device, sustain_s: float = 3.0):
+    """Dense int8 GEMM TOPS via torch._int_mm (cuBLASLt) at 8192^3:
+    (burst = best of 10 single launches, sustained = back-to-back launches
+    for ``sustain_s`` seconds, the rate under the power cap), or None."""
     try:
         n = 8192
         a = torch.randint(-100, 100, (n, n), dtype=torch.int8, device=device)
@@ -306,8 +308,17 @@ def measure_int8_peak(device) -> float | None:
             e.record()
             e.synchronize()
             best = min(best, s.elapsed_time(e) / 1e3)
+        burst = 2.0 * n**3 / best / 1e12
+        reps = max(1, int(sustain_s / best))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            torch._int_mm(a, b)
+        e.record()
+        e.synchronize()
+        sustained = 2.0 * n**3 * reps / (s.elapsed_time(e) / 1e3) / 1e12
         del a, b
-        return 2.0 * n**3 / best / 1e12
+        return burst, sustained
     except Exception:
         return None
 
@@ -396,7 +407,7 @@ def measure_ao2mo(args, rank, world, local):
 def run_ours(args, rank, world, local):
     import trntensor_b200 as tt
     from trntensor_b200 import _lib, distributed
-    from trntensor_b200.dispatch import _cuda_mp2_energy
+    from trntensor_b200.dispatch import _cuda_mp2_energy, pair_offset
     from trntensor_b200.inputs import mp2_inputs
 
     lib = _lib.load()
@@ -461,12 +472,17 @@ def run_ours(args, rank, world, local):
 
     value = args.steps * job_flops / elapsed / 1e12
     # launches per step: one split + the energy kernel issued in chunks of
-    # ~48 waves (same rule as tt_mp2_energy_presplit_i8)
+    # ~48 waves, each chunk as a launch of its two-phase items (if any) and
+    # one of its one-phase items (same rule as tt_mp2_energy_presplit_i8)
     nblk = (nvir + 127) // 128
     ipp = nblk * (nblk + 1) // 2
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     per_launch = max(1, sms * 48 // ipp)
-    energy_launches = -(-(pe - pb) // per_launch)
+    energy_launches = 0
+    for lo in range(pb, pe, per_launch):
+        hi = min(pe, lo + per_launch)
+        diag = sum(1 for i in range(nocc) if lo <= pair_offset(i, nocc) < hi)
+        energy_launches += 1 + (1 if (hi - lo - diag) * (nblk * (nblk - 1) // 2) > 0 else 0)
 
     # sanity check: 8 pairs against the fp64 CUDA-core kernel
     e_chk, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(pb, min(pe, pb + 8)))
@@ -493,16 +509,19 @@ def run_ours(args, rank, world, local):
         torch.cuda.empty_cache()
 
     # roofline of the dominant kernel
-    int8_peak = measure_int8_peak(dev)
+    int8 = measure_int8_peak(dev)
     peaks = measured_peaks()
     bf16 = peaks.get("bf16_tflops")
-    if int8_peak is not None:
-        peak_src = "int8 dense GEMM measured in this run (torch._int_mm, cuBLASLt, 8192^3, best of 10) / 6"
-        peak_eff = int8_peak / 6.0
+    if int8 is not None:
+        int8_burst, int8_peak = int8
+        # the energy kernel runs for seconds under the 1 kW cap: the
+        # denominator is the sustained rate of a plain int8 GEMM
+        peak_src = ("int8 dense GEMM measured in this run (torch._int_mm, cuBLASLt, 8192^3, "
+                    "back to back for 3 s: sustained under the power cap) / 6")
     else:
-        int8_peak = 2.0 * (bf16 or 1590.0)
-        peak_src = "2 x bf16 dense (MEASURED_PEAKS.json) / 6"
-        peak_eff = int8_peak / 6.0
+        int8_burst = int8_peak = 2.0 * (peaks.get("bf16_tflops_sustained") or bf16 or 1375.5)
+        peak_src = "2 x bf16 dense sustained (MEASURED_PEAKS.json) / 6"
+    peak_eff = int8_peak / 6.0
     achieved = my_flops / kernel_s / 1e12
     roof = {
         "bound": "tensor",
@@ -515,6 +534,8 @@ def run_ours(args, rank, world, local):
         "kernel_ms": kernel_s * 1e3,
         "peak_source": peak_src,
         "int8_tops_peak": int8_peak,
+        "int8_tops_burst": int8_burst,
+        "frac_of_burst": achieved / (int8_burst / 6.0),
         "int8_tops_achieved": 6.0 * achieved,
         "flops_per_launch": my_flops,
         "flops_convention": "unique pairs i<=j x 2 nvir^2 naux (fp32-equivalent); the kernel runs 6 int8 slice GEMMs per fp32 GEMM",

@@ -103,6 +103,17 @@ int launch_split(const float* x, float* hi, float* lo, long long rows, int cols,
 
 using namespace tt;
 
+// Number of diagonal pairs (i, i) whose id is below pair id p: the rows i
+// with pair_offset(i) < p (row-major enumeration of i <= j).
+static long long diag_pairs_before(long long p, int n) {
+  long long lo = 0, hi = n;  // smallest i in [0, n] with pair_offset(i) >= p
+  while (lo < hi) {
+    const long long mid = (lo + hi) / 2;
+    if (mp2::pair_offset(mid, n) >= p) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
 // Debug hook: per-CTA wait-cycle counters of TT_MP2_PROFILE builds.
 static long long* g_mp2_prof = nullptr;
 extern "C" void tt_debug_set_profile_buffer(long long* buf) { g_mp2_prof = buf; }
@@ -187,7 +198,7 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
       encode_tmap(&mq_half, Q, 4, dims, strides, box_half, CU_TENSOR_MAP_SWIZZLE_64B,
                   CU_TENSOR_MAP_DATA_TYPE_UINT8))
     return TT_ERR_TMA;
-  mp2::Params p;
+  mp2::Params p{};
   p.scale = scale;
   p.eps_occ = eps_occ;
   p.eps_vir = eps_vir;
@@ -207,22 +218,45 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
   // differ in length); concurrently running items then stop sharing B rows
   // in L2 and the extra HBM traffic costs power and clock. Re-aligning every
   // ~48 waves measured +27-32 % at config 4 (same energy to the last digit).
+  // Each chunk is further issued as one launch of its two-phase items and one
+  // of its one-phase items (p.mode), so that within a launch every item has
+  // the same length.
   constexpr long long kWavesPerLaunch = 48;
   const bool paired = use_paired_kernel();
   const long long ipp = paired ? mp2x2::items_per_pair(p.nblk) : (long long)(p.nblk * (p.nblk + 1) / 2);
   const long long slots = paired ? g_num_sms[dev] / 2 : g_num_sms[dev];
   long long per_launch = slots * kWavesPerLaunch / ipp;
   if (per_launch < 1) per_launch = 1;
-  for (long long lo = pair_begin; lo < pair_end; lo += per_launch) {
-    p.pair_begin = lo;
-    p.pair_end = lo + per_launch < pair_end ? lo + per_launch : pair_end;
-    const long long n_items = (p.pair_end - p.pair_begin) * ipp;
+  const char* sp = std::getenv("TRNTENSOR_B200_MP2_SPLIT_MODES");
+  const bool split_modes = !paired && !(sp != nullptr && sp[0] == '0');
+  const long long nodp = (long long)p.nblk * (p.nblk - 1) / 2;
+  auto launch = [&](long long n_items) -> int {
+    if (n_items <= 0) return TT_OK;
+    p.n_items = n_items;
     const int grid = (int)(n_items < slots ? n_items : slots);
     if (paired)
       mp2x2::energy_kernel<<<2 * grid, mp2x2::kThreads, mp2x2::kSmemBytes, s>>>(mq, mq_half, p);
     else
       mp2::energy_kernel<<<grid, mp2::kThreads, mp2::kSmemBytes, s>>>(mq, p);
-    TT_CUDA(cudaGetLastError());
+    return cuda_status(cudaGetLastError());
+  };
+  for (long long lo = pair_begin; lo < pair_end; lo += per_launch) {
+    const long long hi = lo + per_launch < pair_end ? lo + per_launch : pair_end;
+    p.pair_begin = lo;
+    p.pair_end = hi;
+    if (!split_modes) {
+      p.mode = 0;
+      if ((st = launch((hi - lo) * ipp)) != TT_OK) return st;
+      continue;
+    }
+    // diagonal pairs (i, i) below a pair id = rows whose first pair precedes it
+    const long long d_lo = diag_pairs_before(lo, nocc), d_hi = diag_pairs_before(hi, nocc);
+    p.mode = 1;
+    p.q_begin = lo - d_lo;
+    if ((st = launch(((hi - d_hi) - (lo - d_lo)) * nodp)) != TT_OK) return st;
+    p.mode = 2;
+    p.diag_lo = (int)d_lo;
+    if ((st = launch((hi - lo) * p.nblk + (d_hi - d_lo) * nodp)) != TT_OK) return st;
   }
   return TT_OK;
 }

@@ -59,6 +59,17 @@ struct Params {
   int nocc, nvir, naux_pad;
   long long pair_begin, pair_end;
   int nblk;              // ceil(nvir / 128)
+  // Which (pair, block) items this launch runs (pairs in [pair_begin, pair_end)):
+  //   0: all of them;
+  //   1: the two-phase items only, i < j and A < B (strict pair q_begin on);
+  //   2: the one-phase items only: A == B for every pair, then A < B for the
+  //      i == j pairs, whose rows are diag_lo, diag_lo + 1, ...
+  // Launches of one kind run items of equal length, so the CTAs stay in step
+  // and read the same operand rows at the same time.
+  int mode;
+  long long q_begin;
+  int diag_lo;
+  long long n_items;
   double* energy;
   double* pair_partials;
   int* err;
@@ -85,17 +96,48 @@ struct Item {
   // T symmetric (y = x), a diagonal block gives y = x^T.
   __device__ bool single() const { return i == j || a0 == b0; }
 };
-__device__ inline Item item_decode(long long w, const Params& p) {
-  const int nbp = p.nblk * (p.nblk + 1) / 2;
-  Item it;
-  pair_decode(p.pair_begin + w / nbp, p.nocc, it.i, it.j);
-  int r = (int)(w % nbp), A = 0;
-  while (r >= p.nblk - A) {
-    r -= p.nblk - A;
+// A < B from its row-major index among the nblk (nblk - 1) / 2 off-diagonal blocks
+__device__ inline void offdiag_decode(int r, int nblk, int& A, int& B) {
+  A = 0;
+  while (r >= nblk - 1 - A) {
+    r -= nblk - 1 - A;
     ++A;
   }
+  B = A + 1 + r;
+}
+__device__ inline Item item_decode(long long w, const Params& p) {
+  Item it;
+  int A = 0, B = 0;
+  if (p.mode == 1) {
+    const int nodp = p.nblk * (p.nblk - 1) / 2;
+    // strict pairs i < j of n rows enumerate like pairs i <= j' of n - 1 rows
+    int jj;
+    pair_decode(p.q_begin + w / nodp, p.nocc - 1, it.i, jj);
+    it.j = jj + 1;
+    offdiag_decode((int)(w % nodp), p.nblk, A, B);
+  } else if (p.mode == 2) {
+    const long long nd = (p.pair_end - p.pair_begin) * p.nblk;
+    if (w < nd) {
+      pair_decode(p.pair_begin + w / p.nblk, p.nocc, it.i, it.j);
+      A = B = (int)(w % p.nblk);
+    } else {
+      const int nodp = p.nblk * (p.nblk - 1) / 2;
+      w -= nd;
+      it.i = it.j = p.diag_lo + (int)(w / nodp);
+      offdiag_decode((int)(w % nodp), p.nblk, A, B);
+    }
+  } else {
+    const int nbp = p.nblk * (p.nblk + 1) / 2;
+    pair_decode(p.pair_begin + w / nbp, p.nocc, it.i, it.j);
+    int r = (int)(w % nbp);
+    while (r >= p.nblk - A) {
+      r -= p.nblk - A;
+      ++A;
+    }
+    B = A + r;
+  }
   it.a0 = A * kBlk;
-  it.b0 = (A + r) * kBlk;
+  it.b0 = B * kBlk;
   return it;
 }
 
@@ -115,8 +157,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
   double* red = (double*)(tmem_slot + 2);  // kEpiWarps doubles
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nbp = p.nblk * (p.nblk + 1) / 2;
-  const long long n_items = (p.pair_end - p.pair_begin) * (long long)nbp;
+  const long long n_items = p.n_items;
   const int nkc = p.naux_pad / kKC;
 
   if (threadIdx.x == 0) {
