@@ -162,3 +162,30 @@ def test_step1_on_chip_split_matches_preslice(cuda_ok, shape, monkeypatch):
     b = _cuda_ao_to_mo_transform(eri, co, cv).cpu().numpy()
     assert max_rel(a, ref) <= TOL_F32
     assert max_rel(b, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("shape", [(256, 130, 100, 64), (520, 16, 40, 200), (1024, 128, 96, 160)])
+def test_step1_fused_scales_match_column_pass(cuda_ok, shape, monkeypatch):
+    """Step 1 computes eri's column scales inside the GEMM (a max pass over the
+    next tile's strip while the current tile converts); the separate column-max
+    pass (TRNTENSOR_B200_AO2MO_COLMAX=1) uses the same scale rule, so both give
+    bit-identical tensors. nocc = 130 gives two row tiles per strip, nbf = 520
+    a ragged last k-chunk, and the last shape more tiles than CTAs."""
+    from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
+
+    nbf, nocc, nvir, naux = shape
+    g = torch.Generator().manual_seed(nbf + naux)
+    eri = (torch.randn(nbf, nbf, naux, generator=g) * 0.1).cuda()
+    # columns of very different magnitude, so that a wrong scale would show
+    eri *= torch.logspace(-3, 3, naux, device="cuda")
+    co = torch.randn(nbf, nocc, generator=g).cuda()
+    cv = torch.randn(nbf, nvir, generator=g).cuda()
+    fused = _cuda_ao_to_mo_transform(eri, co, cv)
+    fused2 = _cuda_ao_to_mo_transform(eri, co, cv)
+    monkeypatch.setenv("TRNTENSOR_B200_AO2MO_COLMAX", "1")
+    sep = _cuda_ao_to_mo_transform(eri, co, cv)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, sep)
+    assert torch.equal(fused, fused2)
+    ref = _cuda_ao_to_mo_transform(eri.double(), co.double(), cv.double()).cpu().numpy()
+    assert max_rel(fused.cpu().numpy(), ref) <= TOL_F32

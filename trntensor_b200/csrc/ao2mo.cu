@@ -17,7 +17,11 @@ int setup(int dev) {
   return once_per_device(g_flags, g_ok, dev, [dev]() -> int {
     if (cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return TT_ERR_CUDA;
-    if (cudaFuncSetAttribute(ozc::gemm_cvt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(ozc::gemm_cvt_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             ozc::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(ozc::gemm_cvt_kernel<true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ozc::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
     if (cudaFuncSetAttribute(oz::gemm_kernel<false, false>,
@@ -203,11 +207,17 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
                       dev_status, s, sms)))
       return st;
   } else {
-    // column scales of eri only; the GEMM splits fp32 eri tiles on chip
-    const long long nblk = (pe + oz::kSplitCols - 1) / oz::kSplitCols;
-    const int g = (int)(nblk < (long long)sms * 8 ? nblk : (long long)sms * 8);
-    oz::colmax_kernel<<<g, oz::kSplitThreads, 0, s>>>(eri, ncol, 0, 1, nbf, nbf * naux, pe, se);
-    if ((st = cuda_status(cudaGetLastError()))) return st;
+    // The GEMM splits fp32 eri tiles on chip. Its column scales come from the
+    // GEMM itself (one HBM read of eri) when the contraction has more than two
+    // 64-row chunks, else from a separate column-max pass.
+    const char* cm = std::getenv("TRNTENSOR_B200_AO2MO_COLMAX");
+    const bool fuse = nbf > 2 * ozc::kKC && !(cm != nullptr && cm[0] == '1');
+    if (!fuse) {
+      const long long nblk = (pe + oz::kSplitCols - 1) / oz::kSplitCols;
+      const int g = (int)(nblk < (long long)sms * 8 ? nblk : (long long)sms * 8);
+      oz::colmax_kernel<<<g, oz::kSplitThreads, 0, s>>>(eri, ncol, 0, 1, nbf, nbf * naux, pe, se);
+      if ((st = cuda_status(cudaGetLastError()))) return st;
+    }
     CUtensorMap ma, mx;
     const uint64_t xd[2] = {(uint64_t)ncol, (uint64_t)nbf};
     const uint64_t xs[1] = {(uint64_t)ncol * 4};
@@ -227,9 +237,14 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     pc.tiles_n = (int)((ncol + ozc::kTile - 1) / ozc::kTile);
     pc.err = dev_status;
     pc.prof = g_ozc_prof;
+    const char* hint = std::getenv("TRNTENSOR_B200_AO2MO_L2HINT");
+    pc.l2hint = !(hint != nullptr && hint[0] == '0');  // on unless set to 0
     const long long tiles = (long long)pc.tiles_m * pc.tiles_n;
     const int grid = (int)(tiles < sms ? tiles : sms);
-    ozc::gemm_cvt_kernel<<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
+    if (fuse)
+      ozc::gemm_cvt_kernel<true><<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
+    else
+      ozc::gemm_cvt_kernel<false><<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
     if ((st = cuda_status(cudaGetLastError()))) return st;
   }
   // slices of inter[i] (K = n, N = P), scales per (i, P)

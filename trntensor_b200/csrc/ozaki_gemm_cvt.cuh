@@ -2,9 +2,14 @@
 //   C[m][n] = sum_k A[k][m] X[k][n]
 // A: int8 Ozaki slices of C_occ (MN-major, as in ozaki_gemm.cuh), kARep
 //    identical copies;
-// X: fp32 rows (eri viewed as nbf x nbf*naux), read once by TMA in
-//    64 x 128 tiles and split in shared memory, with the column scales s_n
-//    (max over all k) computed beforehand by colmax_kernel.
+// X: fp32 rows (eri viewed as nbf x nbf*naux), read by TMA in 64 x 128
+//    tiles and split in shared memory. The column scales s_n (max over all k)
+//    come either from colmax_kernel (kFuse = false) or from the kernel itself
+//    (kFuse = true): each CTA streams the whole K x 128 strip of its NEXT
+//    tile through the fp32 ring once for the column maxima while it converts
+//    its current tile, whose strip it read the same way one tile earlier and
+//    now re-reads from L2 (148 CTAs x 512 KB strips at nbf = 1024, well
+//    inside the 126 MB L2). eri then crosses HBM once instead of twice.
 // This removes the separate slice pass and its 3 bytes/element round trip
 // through HBM. Two rings in shared memory:
 //   fp32 landing ring (3 x 32 KB): one producer warp's TMA fills X tiles;
@@ -51,19 +56,25 @@ constexpr int kQLd = kQCols + 4;
 constexpr int kColPark = 3 * kTile;           // TMEM columns of the parked fp32 tile
 constexpr int kARep = 8;                      // copies of the A slices (CTA b reads copy b % kARep)
 constexpr int kOutBytes = kTile * kQLd * 4;
-constexpr int kSmemBytes = kFStages * kFBytes + kIStages * kIBytes + kOutBytes + kTile * 4 + 1024 + 256;
+constexpr int kCMaxBytes = kCvtWarps * kTile * 4;  // per-warp column maxima (fused scales)
+constexpr int kSmemBytes = kFStages * kFBytes + kIStages * kIBytes + kOutBytes + 2 * kTile * 4 +
+                           kCMaxBytes + 1024 + 256;
+constexpr int kCvtBar = 2;  // named barrier of the converter warps
 
 struct Params {
   const float* sA;    // column scales of A (per m)
-  const float* sX;    // column scales of X (per n), from colmax_kernel
+  const float* sX;    // column scales of X (per n), from colmax_kernel; unused when kFuse
   float* C;
   long long ldc;
   int M, N, K;
   int tiles_m, tiles_n;
   int* err;
   long long* prof;  // optional per-CTA wait-cycle counters (TT_OZC_PROFILE builds)
+  int l2hint;       // kFuse: keep max-pass lines in L2 (evict_last) for the conversion
+                    // re-read, which marks them evict_first; output stores streaming
 };
 
+template <bool kFuse>
 static __global__ void __launch_bounds__(kThreads, 1)
     gemm_cvt_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX,
                     Params p) {
@@ -72,8 +83,9 @@ static __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* fring = smem;
   uint8_t* iring = smem + kFStages * kFBytes;
   float* ostage = (float*)(iring + kIStages * kIBytes);
-  float* escale = (float*)((uint8_t*)ostage + kOutBytes);  // column scales of the tile
-  uint64_t* fullF = (uint64_t*)(escale + kTile);
+  float* escale = (float*)((uint8_t*)ostage + kOutBytes);  // column scales, [2][kTile]
+  float* cmax = escale + 2 * kTile;                         // [kCvtWarps][kTile] (kFuse)
+  uint64_t* fullF = (uint64_t*)(cmax + kCvtWarps * kTile);
   uint64_t* freeF = fullF + kFStages;
   uint64_t* fullA = freeF + kFStages;
   uint64_t* conv = fullA + kIStages;
@@ -81,7 +93,8 @@ static __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = emptyI + kIStages;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* final_bar = acc_empty + 1;
-  uint32_t* tmem_slot = (uint32_t*)(final_bar + 1);
+  uint64_t* scale_full = final_bar + 1;  // [2]: tile scales ready (kFuse), by tile parity
+  uint32_t* tmem_slot = (uint32_t*)(scale_full + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long n_tiles = (long long)p.tiles_m * p.tiles_n;
@@ -100,6 +113,8 @@ static __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 32 * kEpiWarps);
     mbar_init(final_bar, 1);
+    mbar_init(&scale_full[0], 32);
+    mbar_init(&scale_full[1], 32);
     fence_mbar_init();
     tma_prefetch_desc(&mapA);
     tma_prefetch_desc(&mapX);
@@ -129,22 +144,41 @@ static __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* fill_bar = fp32 ? fullF : fullA;
       uint32_t it = 0;
       bool ok = true;
-      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
+      const uint64_t keep = l2_policy_evict_last(), drop = l2_policy_evict_first();
+      // one ring slot: wait for it, then fill it with chunk kc of tile w
+      // (max_pass: the first of the strip's two reads)
+      auto issue = [&](long long w, int kc, bool max_pass) {
+        if (!ok) return;
         int m0, n0;
         tile_of(w, m0, n0);
-        for (int kc = 0; kc < nkc; ++kc, ++it) {
-          const int s = it % nst;
-          if (!mbar_wait(&wait_bar[s], ((it / nst) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
-            ok = false;
-            break;
-          }
-          if (fp32) {
-            mbar_arrive_expect_tx(&fill_bar[s], kFBytes);
+        const int s = it % nst;
+        if (!mbar_wait(&wait_bar[s], ((it / nst) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
+          ok = false;
+          return;
+        }
+        if (fp32) {
+          mbar_arrive_expect_tx(&fill_bar[s], kFBytes);
+          if (kFuse && p.l2hint)
+            tma_load_2d_hint(fring + s * kFBytes, &mapX, &fill_bar[s], n0, kc * kKC,
+                             max_pass ? keep : drop);
+          else
             tma_load_2d(fring + s * kFBytes, &mapX, &fill_bar[s], n0, kc * kKC);
-          } else {
-            mbar_arrive_expect_tx(&fill_bar[s], kARegion);
-            tma_load_4d(iring + s * kIBytes, &mapA, &fill_bar[s], m0, kc * kKC, blockIdx.x % kARep, 0);
-          }
+        } else {
+          mbar_arrive_expect_tx(&fill_bar[s], kARegion);
+          tma_load_4d(iring + s * kIBytes, &mapA, &fill_bar[s], m0, kc * kKC, blockIdx.x % kARep, 0);
+        }
+        ++it;
+      };
+      // fused scales: the fp32 stream is the first tile's strip (maxima), then
+      // per tile the chunks of the next tile's strip (maxima) interleaved with
+      // the current tile's (conversion), in the order the converters take them
+      if (kFuse && fp32 && blockIdx.x < n_tiles)
+        for (int kc = 0; kc < nkc; ++kc) issue(blockIdx.x, kc, true);
+      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
+        const long long nxt = w + gridDim.x;
+        for (int kc = 0; kc < nkc; ++kc) {
+          issue(w, kc, false);
+          if (kFuse && fp32 && nxt < n_tiles) issue(nxt, kc, true);
         }
       }
       const uint32_t issued = it;
@@ -237,13 +271,17 @@ static __global__ void __launch_bounds__(kThreads, 1)
     for (long long w = blockIdx.x; w < n_tiles; w += gridDim.x, ++round) {
       int m0, n0;
       tile_of(w, m0, n0);
-      // stage the tile's column scales while the MMAs run
-      if (ew < 4) {
+      // stage the tile's column scales while the MMAs run (kFuse: the
+      // converters computed them into escale[round & 1])
+      const float* esc = escale + (kFuse ? (round & 1u) * kTile : 0);
+      if (!kFuse && ew < 4) {
         const int n = n0 + ew * 32 + lane;
         escale[ew * 32 + lane] = n < p.N ? __ldg(p.sX + n) : 0.f;
       }
-      if (!group_all<32 * kEpiWarps, 1>(mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc)))
-        break;
+      bool got = mbar_wait(acc_full, round & 1u, p.err, kDevTimeoutAcc);
+      if (kFuse && got)
+        got = mbar_wait(&scale_full[round & 1u], (round >> 1) & 1u, p.err, kDevTimeoutFull);
+      if (!group_all<32 * kEpiWarps, 1>(got)) break;
       tc_fence_after();
       const int m = m0 + row;
       const float sa = m < p.M ? __ldg(p.sA + m) : 0.f;
@@ -258,7 +296,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         float v[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * escale[c + k]);
+        for (int k = 0; k < 16; ++k) v[k] = level_combine(l2[k], l3[k], l4[k]) * (sa * esc[c + k]);
         tmem_st16(lane_base + kColPark + c, v);
       }
       tmem_st_wait();
@@ -287,7 +325,11 @@ static __global__ void __launch_bounds__(kThreads, 1)
           float* crow = p.C + (long long)mm * p.ldc + n0 + c0;
           const float* srow = ostage + r * kQLd;
           if (vec && ncols >= kQCols) {
-            reinterpret_cast<float4*>(crow)[l4] = reinterpret_cast<const float4*>(srow)[l4];
+            const float4 v = reinterpret_cast<const float4*>(srow)[l4];
+            if (kFuse && p.l2hint)
+              __stcs(reinterpret_cast<float4*>(crow) + l4, v);
+            else
+              reinterpret_cast<float4*>(crow)[l4] = v;
           } else {
             for (int c = l4; c < ncols && c < kQCols; c += 4) crow[c] = srow[c];
           }
@@ -299,35 +341,92 @@ static __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------------------- converters
     const int cw = warp - (2 + kEpiWarps);
     constexpr int kRows = kKC / kCvtWarps;  // 8 rows per warp and stage
-    uint32_t it = 0;
+    uint32_t itF = 0, itI = 0;  // fp32 ring and int8 ring positions
     bool ok = true;
 #ifdef TT_OZC_PROFILE
     long long w_f = 0, w_e = 0;
 #endif
-    for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
-      int m0, n0;
-      tile_of(w, m0, n0);
-      float inv[4];
+    float inv[4];  // 2^16 / s_n of this lane's four columns of the current tile
+    float mx[4];   // running |max| of the same columns of the next tile (kFuse)
+    // Wait for the next fp32 slot; false (and nothing to read) after an error.
+    auto wait_f = [&]() -> bool {
+#ifdef TT_OZC_PROFILE
+      const long long t0 = clock64();
+#endif
+      if (ok && !mbar_wait(&fullF[itF % kFStages], (itF / kFStages) & 1u, p.err, kDevTimeoutFull))
+        ok = false;
+#ifdef TT_OZC_PROFILE
+      w_f += clock64() - t0;
+#endif
+      return ok;
+    };
+    auto release_f = [&]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&freeF[itF % kFStages]);
+      ++itF;
+    };
+    // One fp32 chunk of the next tile's strip folded into the column maxima.
+    auto max_chunk = [&]() {
+      if (!wait_f()) return;
+      const float4* src = reinterpret_cast<const float4*>(fring + (itF % kFStages) * kFBytes);
+#pragma unroll
+      for (int j = 0; j < kRows; ++j) {
+        const float4 v = src[(cw + kCvtWarps * j) * (kTile / 4) + lane];
+        mx[0] = ozd::absmax(mx[0], v.x);
+        mx[1] = ozd::absmax(mx[1], v.y);
+        mx[2] = ozd::absmax(mx[2], v.z);
+        mx[3] = ozd::absmax(mx[3], v.w);
+      }
+      release_f();
+    };
+    // Column maxima of all converter warps -> scales of the tile with parity
+    // `par`: inv for the converters, escale[par] + scale_full[par] for the
+    // epilogue. Every converter thread calls this (it holds named barriers).
+    auto finish_scales = [&](uint32_t par) -> bool {
+      reinterpret_cast<float4*>(cmax)[cw * 32 + lane] = make_float4(mx[0], mx[1], mx[2], mx[3]);
+      if (!group_all<32 * kCvtWarps, kCvtBar>(ok)) return false;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int n = n0 + 4 * lane + k;
-        const float sc = n < p.N ? __ldg(p.sX + n) : 0.f;
+        float m = 0.f;
+#pragma unroll
+        for (int v = 0; v < kCvtWarps; ++v) m = fmaxf(m, cmax[v * kTile + 4 * lane + k]);
+        const float sc = ozd::scale_for_max(m);
         inv[k] = ozd::inv_scale(sc);
+        if (cw == 0) escale[par * kTile + 4 * lane + k] = sc;
       }
-      for (int kc = 0; kc < nkc; ++kc, ++it) {
-        const int f = it % kFStages, s = it % kIStages;
-#ifdef TT_OZC_PROFILE
-        long long t0 = clock64();
-#endif
-        if (!mbar_wait(&fullF[f], (it / kFStages) & 1u, p.err, kDevTimeoutFull)) {
-          ok = false;
-          break;
+      if (cw == 0) mbar_arrive(&scale_full[par]);
+      group_sync<32 * kCvtWarps, kCvtBar>();  // cmax free for the next tile
+      return true;
+    };
+    // kFuse requires K > 2 * kKC: then a converter that finishes tile r + 1
+    // (and writes the scales of tile r + 2 into escale[r & 1]) has waited for
+    // an int8 slot that the MMA freed inside tile r + 1, so the epilogue has
+    // already read escale[r & 1] and waited on scale_full[r & 1] for tile r.
+    if (kFuse && blockIdx.x < n_tiles) {
+      mx[0] = mx[1] = mx[2] = mx[3] = 0.f;
+      for (int kc = 0; kc < nkc; ++kc) max_chunk();
+      if (!finish_scales(0)) ok = false;
+    }
+    uint32_t round = 0;
+    for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x, ++round) {
+      int m0, n0;
+      tile_of(w, m0, n0);
+      const bool next = kFuse && w + gridDim.x < n_tiles;
+      if (!kFuse) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int n = n0 + 4 * lane + k;
+          const float sc = n < p.N ? __ldg(p.sX + n) : 0.f;
+          inv[k] = ozd::inv_scale(sc);
         }
-#ifdef TT_OZC_PROFILE
-        long long t1 = clock64();
-        w_f += t1 - t0;
-#endif
-        const float4* src = reinterpret_cast<const float4*>(fring + f * kFBytes);
+      }
+      mx[0] = mx[1] = mx[2] = mx[3] = 0.f;
+      for (int kc = 0; kc < nkc; ++kc) {
+        const int s = itI % kIStages;
+        const uint32_t ph = (itI / kIStages) & 1u;
+        ++itI;
+        if (!wait_f()) continue;  // error: run on without waiting, to the next group_all
+        const float4* src = reinterpret_cast<const float4*>(fring + (itF % kFStages) * kFBytes);
         // Split this warp's rows into registers first: the byte permutes
         // consume every loaded value, so once all lanes are past them (the
         // __syncwarp) no read of the slot is outstanding and it can be refilled.
@@ -338,14 +437,13 @@ static __global__ void __launch_bounds__(kThreads, 1)
           const float x4[4] = {v.x, v.y, v.z, v.w};
           ozd::split4(x4, inv, q[j][0], q[j][1], q[j][2]);  // one FMA per value
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&freeF[f]);  // this warp's rows are consumed
+        release_f();  // this warp's rows are consumed
 #ifdef TT_OZC_PROFILE
         long long t2 = clock64();
 #endif
-        if (!mbar_wait(&emptyI[s], ((it / kIStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
+        if (!mbar_wait(&emptyI[s], ph ^ 1u, p.err, kDevTimeoutEmpty)) {
           ok = false;
-          break;
+          continue;
         }
 #ifdef TT_OZC_PROFILE
         w_e += clock64() - t2;
@@ -366,7 +464,9 @@ static __global__ void __launch_bounds__(kThreads, 1)
         // and arrives (conv counts every converter thread)
         fence_proxy_async_smem();
         mbar_arrive(&conv[s]);
+        if (next) max_chunk();  // the producer queued it right after this chunk
       }
+      if (next && !finish_scales((round + 1) & 1u)) ok = false;
     }
 #ifdef TT_OZC_PROFILE
     if (p.prof && cw == 0 && lane == 0) {
