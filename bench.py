@@ -486,25 +486,39 @@ def run_ours(args, rank, world, local):
 
     # sanity check: 8 pairs against the fp64 CUDA-core kernel
     e_chk, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(pb, min(pe, pb + 8)))
-    e_ref, _ = _cuda_mp2_energy(B.double(), eo.double(), ev.double(), pair_range=(pb, min(pe, pb + 8)))
+    e_ref, _ = _cuda_mp2_energy(B.double(), eo.double(), ev.double(),
+                                pair_range=(pb, min(pe, pb + 8)), kernel="simt")
     check_rel = abs(e_chk.item() - e_ref.item()) / abs(e_ref.item())
 
-    # fp64 path (precision="kahan"): rate on a 256-pair slice of the same workload
+    # fp64 path (precision="kahan"): rate on a slice of the same workload, for
+    # the five-digit int8 tensor-core kernel (split included) and the CUDA-core
+    # fp64 kernel
     fp64 = None
     if rank == 0:
         Bd, eod, evd = B.double(), eo.double(), ev.double()
-        rng = (pb, min(pe, pb + 256))
-        _cuda_mp2_energy(Bd, eod, evd, pair_range=(rng[0], rng[0] + 2))
-        a64, b64 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a64.record()
-        _cuda_mp2_energy(Bd, eod, evd, pair_range=rng)
-        b64.record()
-        torch.cuda.synchronize(dev)
-        t64 = a64.elapsed_time(b64) / 1e3
-        n64 = rng[1] - rng[0]
-        fp64 = {"pairs": n64, "TFLOP_per_s": n64 * flops_per_pair(c) / t64 / 1e12,
-                "full_config_estimate_s": npairs / n64 * t64,
-                "kernel": "tt::mp2s::energy_kernel<double> (CUDA cores, fp64 throughout)"}
+
+        def rate64(kernel, n):
+            rng = (pb, min(pe, pb + n))
+            _cuda_mp2_energy(Bd, eod, evd, pair_range=(rng[0], rng[0] + 2), kernel=kernel)
+            a64, b64 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a64.record()
+            e64, _ = _cuda_mp2_energy(Bd, eod, evd, pair_range=rng, kernel=kernel)
+            b64.record()
+            torch.cuda.synchronize(dev)
+            t64 = a64.elapsed_time(b64) / 1e3
+            n64 = rng[1] - rng[0]
+            return n64, t64, e64.item()
+
+        n_tc, t_tc, e_tc = rate64("tc", 1024)
+        n_s, t_s, e_s = rate64("simt", 128)
+        e_s128, _ = _cuda_mp2_energy(Bd, eod, evd, pair_range=(pb, pb + n_s), kernel="tc")
+        fp64 = {"pairs": n_tc, "TFLOP_per_s": n_tc * flops_per_pair(c) / t_tc / 1e12,
+                "full_config_estimate_s": npairs / n_tc * t_tc,
+                "kernel": "tt::mp2d::energy_kernel (int8 tcgen05, 5-digit Ozaki, fp64 epilogue)",
+                "cuda_core_fp64": {"pairs": n_s,
+                                   "TFLOP_per_s": n_s * flops_per_pair(c) / t_s / 1e12,
+                                   "kernel": "tt::mp2s::energy_kernel<double>"},
+                "rel_diff_tc_vs_cuda_core": abs(e_s128.item() - e_s) / abs(e_s)}
         del Bd, eod, evd
         torch.cuda.empty_cache()
 

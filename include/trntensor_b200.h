@@ -131,8 +131,27 @@ int tt_mp2_energy_f32_noalloc(const float* B, const float* eps_occ, const float*
                               int nocc, int nvir, int naux, double* energy,
                               double* pair_partials, int* dev_status, void* stream);
 
-/* DF-MP2 energy in fp64 throughout (precision="kahan" semantics of
- * trntensor/einsum.py:108-111 applied to trntensor/quantum.py:87-100). */
+/* Workspace of tt_mp2_energy_f64_tc: five int8 digit planes
+ * (5, nocc*nvir, naux padded to 64), fp64 row scales and the per-CTA fp64
+ * scratch tiles of the energy kernel. */
+size_t tt_mp2_f64_workspace_bytes(int nocc, int nvir, int naux);
+
+/* DF-MP2 energy of fp64 inputs on int8 tensor cores (precision="kahan":
+ * trntensor/einsum.py:108-111 applied to trntensor/quantum.py:87-100; replaces
+ * the fp64 route through trntensor/nki/dispatch.py:240-283). Five-digit Ozaki
+ * split of B's rows, 19 exact int8 GEMMs per pair block, energy terms in fp64;
+ * |dE|/|E| ~ 1e-14. naux padded to 64 must be <= 32767 (TT_ERR_SHAPE
+ * otherwise). Same pair-range, energy, partials and dev_status contract as
+ * tt_mp2_energy_f32. */
+int tt_mp2_energy_f64_tc(const double* B, const double* eps_occ, const double* eps_vir,
+                         int nocc, int nvir, int naux, long long pair_begin, long long pair_end,
+                         void* workspace, size_t workspace_bytes, double* energy,
+                         double* pair_partials, int* dev_status, void* stream);
+
+/* DF-MP2 energy in fp64 throughout on CUDA cores (precision="kahan"
+ * semantics of trntensor/einsum.py:108-111 applied to
+ * trntensor/quantum.py:87-100); the fp64 path for naux beyond the limit of
+ * tt_mp2_energy_f64_tc and an independent check of it. */
 int tt_mp2_energy_f64(const double* B, const double* eps_occ, const double* eps_vir, int nocc,
                       int nvir, int naux, long long pair_begin, long long pair_end,
                       double* energy, double* pair_partials, void* stream);

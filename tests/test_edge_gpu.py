@@ -100,6 +100,23 @@ def test_nonfinite_input_propagates(cuda_ok, bad):
     B[2, 31, 5] = bad
     e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
     assert not np.isfinite(e.item())
+    e64 = tt.mp2_energy(B.double().cuda(), eo.double().cuda(), ev.double().cuda())
+    assert not np.isfinite(e64.item())
+
+
+def test_fp64_zero_rows_and_extreme_magnitudes(cuda_ok):
+    """fp64 tensor-core path: zero rows contribute nothing, and rows whose
+    magnitudes differ by 1e+-20 (each row has its own power-of-two scale)
+    stay at fp64 accuracy."""
+    B, eo, ev = mp2_inputs(4, 150, 70, seed=5)
+    B = B.double()
+    B[1] = 0
+    B[0, 7] = 0
+    B[2, :50] *= 1e20
+    B[3, 60:] *= 1e-20
+    ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.double().numpy(), ev.double().numpy())
+    e = tt.mp2_energy(B.cuda(), eo.double().cuda(), ev.double().cuda())
+    assert np.isfinite(e.item()) and rel(e.item(), ref) <= 1e-12
 
 
 def test_nonfinite_eri_propagates(cuda_ok):

@@ -152,6 +152,26 @@ def test_config4_sampled_pairs(cuda_ok):
         assert rel(part[i, j].item(), ref) <= 1e-6
 
 
+@pytest.mark.parametrize("shape", [(256, 1792, 6144), (5, 300, 1000), (3, 129, 32704)])
+def test_fp64_tensor_core_vs_cuda_core(cuda_ok, shape):
+    """fp64 energy (precision="kahan"): the five-digit int8 tensor-core kernel
+    and the CUDA-core fp64 kernel agree to 1e-12 on every pair kind (i == j,
+    i < j, diagonal and off-diagonal blocks) and in the per-pair partials;
+    config 4 is checked on pair ranges; naux 32704 is the longest contraction
+    the int32 sums allow."""
+    nocc, nvir, naux = shape
+    B, eo, ev = mp2_inputs(nocc, nvir, naux, seed=21, device="cuda")
+    B, eo, ev = B.double(), eo.double(), ev.double()
+    npairs = nocc * (nocc + 1) // 2
+    ranges = [(0, npairs)] if npairs <= 64 else [(0, 3), (255, 260), (npairs - 4, npairs)]
+    for rng in ranges:
+        e_tc, p_tc = _cuda_mp2_energy(B, eo, ev, pair_range=rng, return_partials=True)
+        e_s, p_s = _cuda_mp2_energy(B, eo, ev, pair_range=rng, return_partials=True,
+                                    kernel="simt")
+        assert rel(e_tc.item(), e_s.item()) <= RTOL_F64
+        torch.testing.assert_close(p_tc, p_s, rtol=1e-11, atol=1e-14 * p_s.abs().max().item())
+
+
 def test_ozaki_split_is_exact_to_22_bits(cuda_ok):
     """tt_split_i8: x == s (q1 + q2/2^8 + q3/2^16) up to half a unit of the last slice."""
     lib = _lib.load()

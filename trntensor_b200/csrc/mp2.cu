@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include "mp2_i8.cuh"
 #include "mp2_i8_2sm.cuh"
+#include "mp2_i8x5.cuh"
 #include "mp2_simt.cuh"
 #include "mp2_tf32.cuh"
 
@@ -48,6 +49,9 @@ int mp2_setup(int dev) {
   return once_per_device(g_mp2_attr_flags, g_mp2_attr_ok, dev, [dev]() -> int {
     if (cudaFuncSetAttribute(mp2::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              mp2::kSmemBytes) != cudaSuccess)
+      return TT_ERR_CUDA;
+    if (cudaFuncSetAttribute(mp2d::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mp2d::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
     if (cudaFuncSetAttribute(mp2x2::energy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              mp2x2::kSmemBytes) != cudaSuccess)
@@ -112,6 +116,37 @@ static long long diag_pairs_before(long long p, int n) {
     if (mp2::pair_offset(mid, n) >= p) hi = mid; else lo = mid + 1;
   }
   return lo;
+}
+
+// Issues the pair range [pair_begin, pair_end) as consecutive launches of
+// per_launch pairs. With split_modes each chunk is one launch of its
+// two-phase items (mode 1) and one of its one-phase items (mode 2), so that
+// every item of a launch has the same length; else one launch of all of
+// them (mode 0). launch(n_items) runs the kernel on p as set here.
+template <class Launch>
+static int launch_chunks(mp2::Params& p, long long pair_begin, long long pair_end,
+                         long long per_launch, long long ipp, bool split_modes, Launch&& launch) {
+  const long long nodp = (long long)p.nblk * (p.nblk - 1) / 2;
+  int st = TT_OK;
+  for (long long lo = pair_begin; lo < pair_end; lo += per_launch) {
+    const long long hi = lo + per_launch < pair_end ? lo + per_launch : pair_end;
+    p.pair_begin = lo;
+    p.pair_end = hi;
+    if (!split_modes) {
+      p.mode = 0;
+      if ((st = launch((hi - lo) * ipp)) != TT_OK) return st;
+      continue;
+    }
+    // diagonal pairs (i, i) below a pair id = rows whose first pair precedes it
+    const long long d_lo = diag_pairs_before(lo, p.nocc), d_hi = diag_pairs_before(hi, p.nocc);
+    p.mode = 1;
+    p.q_begin = lo - d_lo;
+    if ((st = launch(((hi - d_hi) - (lo - d_lo)) * nodp)) != TT_OK) return st;
+    p.mode = 2;
+    p.diag_lo = (int)d_lo;
+    if ((st = launch((hi - lo) * p.nblk + (d_hi - d_lo) * nodp)) != TT_OK) return st;
+  }
+  return TT_OK;
 }
 
 // Debug hook: per-CTA wait-cycle counters of TT_MP2_PROFILE builds.
@@ -229,7 +264,6 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
   if (per_launch < 1) per_launch = 1;
   const char* sp = std::getenv("TRNTENSOR_B200_MP2_SPLIT_MODES");
   const bool split_modes = !paired && !(sp != nullptr && sp[0] == '0');
-  const long long nodp = (long long)p.nblk * (p.nblk - 1) / 2;
   auto launch = [&](long long n_items) -> int {
     if (n_items <= 0) return TT_OK;
     p.n_items = n_items;
@@ -240,25 +274,7 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
       mp2::energy_kernel<<<grid, mp2::kThreads, mp2::kSmemBytes, s>>>(mq, p);
     return cuda_status(cudaGetLastError());
   };
-  for (long long lo = pair_begin; lo < pair_end; lo += per_launch) {
-    const long long hi = lo + per_launch < pair_end ? lo + per_launch : pair_end;
-    p.pair_begin = lo;
-    p.pair_end = hi;
-    if (!split_modes) {
-      p.mode = 0;
-      if ((st = launch((hi - lo) * ipp)) != TT_OK) return st;
-      continue;
-    }
-    // diagonal pairs (i, i) below a pair id = rows whose first pair precedes it
-    const long long d_lo = diag_pairs_before(lo, nocc), d_hi = diag_pairs_before(hi, nocc);
-    p.mode = 1;
-    p.q_begin = lo - d_lo;
-    if ((st = launch(((hi - d_hi) - (lo - d_lo)) * nodp)) != TT_OK) return st;
-    p.mode = 2;
-    p.diag_lo = (int)d_lo;
-    if ((st = launch((hi - lo) * p.nblk + (d_hi - d_lo) * nodp)) != TT_OK) return st;
-  }
-  return TT_OK;
+  return launch_chunks(p, pair_begin, pair_end, per_launch, ipp, split_modes, launch);
 }
 
 int tt_split_tf32(const float* x, float* hi, float* lo, long long rows, int cols, int cols_pad,
@@ -346,6 +362,95 @@ int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir
   if (st != TT_OK) return st;
   return tt_mp2_energy_presplit_i8(q, scale, naux_pad, eps_occ, eps_vir, nocc, nvir, pair_begin,
                                    pair_end, energy, pair_partials, dev_status, stream);
+}
+
+size_t tt_mp2_f64_workspace_bytes(int nocc, int nvir, int naux) {
+  if (nocc <= 0 || nvir <= 0 || naux <= 0) return 0;
+  const size_t rows = (size_t)nocc * (size_t)nvir;
+  return align256((size_t)mp2d::kDigits * rows * (size_t)naux_padded_i8(naux)) +
+         align256(rows * sizeof(double)) +
+         (size_t)mp2d::kMaxGrid * (size_t)mp2d::kScratchDoubles * sizeof(double);
+}
+
+int tt_mp2_energy_f64_tc(const double* B, const double* eps_occ, const double* eps_vir, int nocc,
+                         int nvir, int naux, long long pair_begin, long long pair_end,
+                         void* workspace, size_t workspace_bytes, double* energy,
+                         double* pair_partials, int* dev_status, void* stream) {
+  if (!B || !workspace || !eps_occ || !eps_vir || !energy || !dev_status) return TT_ERR_NULL;
+  if (nocc <= 0 || nvir <= 0 || naux <= 0) return TT_ERR_SHAPE;
+  if (nocc > 65535 || nvir > 65535 || naux_padded_i8(naux) > mp2d::kMaxK) return TT_ERR_SHAPE;
+  if (check_pairs(nocc, pair_begin, pair_end) != TT_OK) return TT_ERR_SHAPE;
+  if (workspace_bytes < tt_mp2_f64_workspace_bytes(nocc, nvir, naux)) return TT_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return TT_ERR_ALIGN;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = mp2_setup(dev);
+  if (st != TT_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int naux_pad = naux_padded_i8(naux);
+  const size_t rows = (size_t)nocc * nvir;
+  const size_t plane = rows * (size_t)naux_pad;
+  int8_t* q = static_cast<int8_t*>(workspace);
+  double* scale = reinterpret_cast<double*>(static_cast<char*>(workspace) +
+                                            align256((size_t)mp2d::kDigits * plane));
+  double* scratch = reinterpret_cast<double*>(reinterpret_cast<char*>(scale) +
+                                              align256(rows * sizeof(double)));
+  TT_CUDA(cudaMemsetAsync(energy, 0, sizeof(double), s));
+  TT_CUDA(cudaMemsetAsync(dev_status, 0, sizeof(int), s));
+  if (pair_partials)
+    TT_CUDA(cudaMemsetAsync(pair_partials, 0, sizeof(double) * (size_t)nocc * nocc, s));
+  if (pair_end == pair_begin) return TT_OK;
+  {
+    long long blocks = ((long long)rows + 7) / 8;
+    const long long cap = (long long)g_num_sms[dev] * 16;
+    if (blocks > cap) blocks = cap;
+    mp2d::split_kernel<<<(unsigned)blocks, 256, 0, s>>>(B, q, scale, (long long)rows, naux,
+                                                        naux_pad, (long long)plane);
+    if ((st = cuda_status(cudaGetLastError())) != TT_OK) return st;
+  }
+  // Digit planes as a 4-D byte tensor (aux, vir, occ, digit), innermost
+  // first; a box is 32 aux x 128 rows x the first 3 (sweep 0) or all 5
+  // (sweep 1) digits, 32B swizzle.
+  CUtensorMap m3, m5;
+  const uint64_t dims[4] = {(uint64_t)naux_pad, (uint64_t)nvir, (uint64_t)nocc,
+                            (uint64_t)mp2d::kDigits};
+  const uint64_t strides[3] = {(uint64_t)naux_pad, (uint64_t)naux_pad * nvir, (uint64_t)plane};
+  const uint32_t box3[4] = {(uint32_t)mp2d::kKC, (uint32_t)mp2d::kBlk, 1, 3};
+  const uint32_t box5[4] = {(uint32_t)mp2d::kKC, (uint32_t)mp2d::kBlk, 1, 5};
+  if (encode_tmap(&m3, q, 4, dims, strides, box3, CU_TENSOR_MAP_SWIZZLE_32B,
+                  CU_TENSOR_MAP_DATA_TYPE_UINT8) ||
+      encode_tmap(&m5, q, 4, dims, strides, box5, CU_TENSOR_MAP_SWIZZLE_32B,
+                  CU_TENSOR_MAP_DATA_TYPE_UINT8))
+    return TT_ERR_TMA;
+  mp2d::Params P{};
+  mp2::Params& p = P.base;
+  p.nocc = nocc;
+  p.nvir = nvir;
+  p.naux_pad = naux_pad;
+  p.nblk = (nvir + mp2d::kBlk - 1) / mp2d::kBlk;
+  p.energy = energy;
+  p.pair_partials = pair_partials;
+  p.err = dev_status;
+  P.scale = scale;
+  P.eps_occ = eps_occ;
+  P.eps_vir = eps_vir;
+  P.scratch = scratch;
+  const long long ipp = (long long)p.nblk * (p.nblk + 1) / 2;
+  const long long slots =
+      g_num_sms[dev] < mp2d::kMaxGrid ? (long long)g_num_sms[dev] : (long long)mp2d::kMaxGrid;
+  // chunks of ~16 waves: an fp64 item issues ~3x the MMAs of an fp32 one,
+  // whose launches are ~48 waves long
+  long long per_launch = slots * 16 / ipp;
+  if (per_launch < 1) per_launch = 1;
+  auto launch = [&](long long n_items) -> int {
+    if (n_items <= 0) return TT_OK;
+    p.n_items = n_items;
+    const int grid = (int)(n_items < slots ? n_items : slots);
+    mp2d::energy_kernel<<<grid, mp2d::kThreads, mp2d::kSmemBytes, s>>>(m3, m5, P);
+    return cuda_status(cudaGetLastError());
+  };
+  return launch_chunks(p, pair_begin, pair_end, per_launch, ipp, true, launch);
 }
 
 }  // extern "C"

@@ -125,7 +125,9 @@ def _cuda_mp2_energy(
     device. ``pair_range`` selects a half-open range of unordered pair ids
     (i <= j, row-major) for sharding. ``kernel`` picks the fp32 kernel:
     ``"tc"`` (int8 Ozaki tensor cores, the product path), ``"simt"`` (CUDA-core
-    fp32 cross-check) or ``"tf32x3"`` (biased 3xTF32 diagnostic).
+    fp32 cross-check) or ``"tf32x3"`` (biased 3xTF32 diagnostic). For fp64
+    (``precision="kahan"``) ``"tc"`` is the five-digit int8 Ozaki kernel and
+    ``"simt"`` the CUDA-core fp64 kernel.
     """
     lib = _lib.load()
     dev = _device()
@@ -151,6 +153,17 @@ def _cuda_mp2_energy(
         torch.empty((nocc, nocc), dtype=torch.float64, device=dev) if return_partials else None
     )
     stream = ctypes.c_void_p(_stream_handle())
+    if cdt == torch.float64 and kernel == "tc" and (naux + 63) // 64 * 64 <= OZAKI_F64_MAX_K:
+        ws_bytes = int(lib.tt_mp2_f64_workspace_bytes(nocc, nvir, naux))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        dev_status = torch.empty((), dtype=torch.int32, device=dev)
+        st = lib.tt_mp2_energy_f64_tc(
+            _ptr(Bd), _ptr(eo), _ptr(ev), nocc, nvir, naux, pb, pe,
+            _ptr(ws), ws_bytes, _ptr(energy), _ptr(partials), _ptr(dev_status), stream,
+        )
+        _lib.check(st, "tt_mp2_energy_f64_tc")
+        _check_status(dev_status, "tt_mp2_energy_f64_tc")
+        return energy, partials
     if cdt == torch.float64:
         st = lib.tt_mp2_energy_f64(
             _ptr(Bd), _ptr(eo), _ptr(ev), nocc, nvir, naux, pb, pe,
@@ -194,6 +207,8 @@ def _cuda_mp2_energy(
 # Longest contraction the int8 Ozaki kernels sum exactly in int32
 # (csrc/ozaki_digits.cuh): K * (64*128 + 128*128 + 128*64) < 2^31.
 OZAKI_MAX_K = 65535
+# The five-digit fp64 kernel (csrc/mp2_i8x5.cuh): K * (2*64*128 + 3*128*128) < 2^31.
+OZAKI_F64_MAX_K = 32767
 
 
 def pair_offset(i: int, nocc: int) -> int:
