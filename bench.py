@@ -43,9 +43,11 @@ CONFIGS = {
     0: dict(nocc=8, nvir=32, naux=96),
 }
 METRIC = "DF-MP2 pair-contraction TFLOP/s"
-# dram__bytes_read.sum + dram__bytes_write.sum of one mp2::energy_kernel launch,
-# from the ncu capture in profiles/mp2_energy_kernel_config4.md, scaled by pairs.
-TRAFFIC_BYTES_PER_LAUNCH = 3.80e12  # 61.1 GB per 528 pairs (ncu, nocc=32) x 32896/528
+# dram__bytes_read.sum + dram__bytes_write.sum of the mp2::energy_kernel
+# launches of one step, per unordered pair: ncu with --cache-control none on
+# the same tiles with nocc = 32 (528 pairs, 16 launches): 74.0 GB per step
+# (profiles/mp2_energy_kernel_config4.md). Traffic grows with the pairs.
+TRAFFIC_BYTES_PER_PAIR = 140.1e6
 
 
 def parse_args():
@@ -537,21 +539,25 @@ def run_ours(args, rank, world, local):
         peak_src = "2 x bf16 dense sustained (MEASURED_PEAKS.json) / 6"
     peak_eff = int8_peak / 6.0
     achieved = my_flops / kernel_s / 1e12
+    # per launch: the step's energy launches average (the ratio is the same)
+    my_pairs = pe - pb
     roof = {
         "bound": "tensor",
         "achieved": achieved,
         "peak": peak_eff,
         "unit": "TFLOP/s",
         "frac": achieved / peak_eff,
-        "traffic": TRAFFIC_BYTES_PER_LAUNCH,
+        "traffic": TRAFFIC_BYTES_PER_PAIR * my_pairs / max(1, energy_launches),
         "kernel": "tt::mp2::energy_kernel",
-        "kernel_ms": kernel_s * 1e3,
+        "launches_per_step": energy_launches,
+        "kernel_ms": kernel_s * 1e3 / max(1, energy_launches),
+        "kernel_ms_per_step": kernel_s * 1e3,
         "peak_source": peak_src,
         "int8_tops_peak": int8_peak,
         "int8_tops_burst": int8_burst,
         "frac_of_burst": achieved / (int8_burst / 6.0),
         "int8_tops_achieved": 6.0 * achieved,
-        "flops_per_launch": my_flops,
+        "flops_per_launch": my_flops / max(1, energy_launches),
         "flops_convention": "unique pairs i<=j x 2 nvir^2 naux (fp32-equivalent); the kernel runs 6 int8 slice GEMMs per fp32 GEMM",
     }
     if bf16:
