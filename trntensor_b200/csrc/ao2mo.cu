@@ -12,6 +12,7 @@ namespace {
 std::once_flag g_flags[kMaxDevices];
 int g_ok[kMaxDevices];
 int g_sms[kMaxDevices];
+int g_split_clusters[kMaxDevices];  // co-resident 2-CTA clusters of gemm_cvt_split_kernel
 
 int setup(int dev) {
   return once_per_device(g_flags, g_ok, dev, [dev]() -> int {
@@ -22,8 +23,30 @@ int setup(int dev) {
                              ozc::kSmemBytes) != cudaSuccess ||
         cudaFuncSetAttribute(ozc::gemm_cvt_kernel<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             ozc::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(ozc::gemm_cvt_split_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ozc::kSmemBytes) != cudaSuccess)
       return TT_ERR_CUDA;
+    {
+      // A persistent grid of more clusters than fit at once would leave a
+      // tail of clusters running alone: size the grid to what is co-resident.
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * 1024, 1, 1);
+      cfg.blockDim = dim3(ozc::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = ozc::kSmemBytes;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, ozc::gemm_cvt_split_kernel, &cfg) != cudaSuccess)
+        return TT_ERR_CUDA;
+      g_split_clusters[dev] = n;
+    }
     if (cudaFuncSetAttribute(oz::gemm_kernel<false, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              oz::kSmemBytes) != cudaSuccess)
@@ -212,6 +235,10 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     // 64-row chunks, else from a separate column-max pass.
     const char* cm = std::getenv("TRNTENSOR_B200_AO2MO_COLMAX");
     const bool fuse = nbf > 2 * ozc::kKC && !(cm != nullptr && cm[0] == '1');
+    // Split-K over CTA pairs (each half needs three k-chunks, as above).
+    const char* sk = std::getenv("TRNTENSOR_B200_AO2MO_SPLITK");
+    const bool split = fuse && nbf > 5 * ozc::kKC && g_split_clusters[dev] > 0 &&
+                       !(sk != nullptr && sk[0] == '0');
     if (!fuse) {
       const long long nblk = (pe + oz::kSplitCols - 1) / oz::kSplitCols;
       const int g = (int)(nblk < (long long)sms * 8 ? nblk : (long long)sms * 8);
@@ -241,7 +268,10 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     pc.l2hint = !(hint != nullptr && hint[0] == '0');  // on unless set to 0
     const long long tiles = (long long)pc.tiles_m * pc.tiles_n;
     const int grid = (int)(tiles < sms ? tiles : sms);
-    if (fuse)
+    if (split) {
+      const long long cl = tiles < g_split_clusters[dev] ? tiles : g_split_clusters[dev];
+      ozc::gemm_cvt_split_kernel<<<(int)(2 * cl), ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
+    } else if (fuse)
       ozc::gemm_cvt_kernel<true><<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
     else
       ozc::gemm_cvt_kernel<false><<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);

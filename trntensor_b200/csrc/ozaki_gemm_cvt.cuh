@@ -32,6 +32,7 @@
 // barrier wait holds up the other).
 #pragma once
 #include "ozaki_gemm.cuh"
+#include "ptx2sm.cuh"
 
 namespace tt {
 namespace ozc {
@@ -47,8 +48,15 @@ constexpr int kIStages = 2;                   // int8 ring (A by TMA, B by conve
 constexpr int kFBytes = kTile * kKC * 4;      // 32 KB fp32 tile
 constexpr int kARegion = 3 * kTile * kKC;     // 24 KB of A slices
 constexpr int kIBytes = 2 * kARegion;         // A and B slices: 48 KB
-constexpr int kEpiWarps = 8;
-constexpr int kCvtWarps = 8;   // (16 converter + 4 epilogue warps measured no faster)
+#ifndef TT_OZC_EPI_WARPS
+#define TT_OZC_EPI_WARPS 8
+#endif
+#ifndef TT_OZC_CVT_WARPS
+#define TT_OZC_CVT_WARPS 8
+#endif
+constexpr int kEpiWarps = TT_OZC_EPI_WARPS;  // 4 or 8: each lane quarter's columns split evenly
+constexpr int kCvtWarps = TT_OZC_CVT_WARPS;  // 8 or 16: divides the 64 rows of a chunk
+constexpr int kEpiCols = kTile * 4 / kEpiWarps;  // columns of one epilogue warp
 constexpr int kAWarp = 2 + kEpiWarps + kCvtWarps;  // A-slice producer (its own warp)
 constexpr int kThreads = 32 * (kAWarp + 1);
 constexpr int kQCols = 16;                    // output staged 16 columns at a time
@@ -58,7 +66,7 @@ constexpr int kARep = 8;                      // copies of the A slices (CTA b r
 constexpr int kOutBytes = kTile * kQLd * 4;
 constexpr int kCMaxBytes = kCvtWarps * kTile * 4;  // per-warp column maxima (fused scales)
 constexpr int kSmemBytes = kFStages * kFBytes + kIStages * kIBytes + kOutBytes + 2 * kTile * 4 +
-                           kCMaxBytes + 1024 + 256;
+                           kCMaxBytes + 2 * kTile * 4 + 1024 + 256;
 constexpr int kCvtBar = 2;  // named barrier of the converter warps
 
 struct Params {
@@ -74,10 +82,54 @@ struct Params {
                     // re-read, which marks them evict_first; output stores streaming
 };
 
-template <bool kFuse>
-static __global__ void __launch_bounds__(kThreads, 1)
-    gemm_cvt_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX,
-                    Params p) {
+// 16-byte store to a shared::cluster address (another CTA's shared memory).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, const float (&v)[4]) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[0]),
+               "f"(v[1]), "f"(v[2]), "f"(v[3])
+               : "memory");
+}
+// red.add of four floats at a 16-byte aligned global address.
+__device__ __forceinline__ void red_add_v4(float* dst, float4 v) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+// Wait on a local mbarrier that the peer CTA of the cluster arrives on
+// (acquire at cluster scope, so that what the peer wrote before arriving is
+// visible), bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const long long t0 = clock64();
+  uint32_t n = 0;
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((++n & 1023u) == 0) {
+      if (*(volatile int*)err != 0) return false;
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// kSplit (with kFuse): a cluster of two CTAs shares each tile and splits its
+// K range in halves, so that each CTA keeps only half a strip (256 KB at
+// nbf = 1024) between its two reads of eri. The column maxima of the halves
+// are exchanged through distributed shared memory (pmax, pfull); rank 0
+// stores its partial tile, then rank 1 adds its own with red.global.add
+// (out_ready / out_done order the two and keep the barriers' phases apart).
+// C = (rank 0 partial) + (rank 1 partial): one fp32 rounding, deterministic.
+template <bool kFuse, bool kSplit>
+__device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUtensorMap& mapX,
+                                              const Params& p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* fring = smem;
@@ -85,7 +137,8 @@ static __global__ void __launch_bounds__(kThreads, 1)
   float* ostage = (float*)(iring + kIStages * kIBytes);
   float* escale = (float*)((uint8_t*)ostage + kOutBytes);  // column scales, [2][kTile]
   float* cmax = escale + 2 * kTile;                         // [kCvtWarps][kTile] (kFuse)
-  uint64_t* fullF = (uint64_t*)(cmax + kCvtWarps * kTile);
+  float* pmax = cmax + kCvtWarps * kTile;                    // [2][kTile] kSplit: the peer's maxima
+  uint64_t* fullF = (uint64_t*)(pmax + 2 * kTile);
   uint64_t* freeF = fullF + kFStages;
   uint64_t* fullA = freeF + kFStages;
   uint64_t* conv = fullA + kIStages;
@@ -94,11 +147,22 @@ static __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* final_bar = acc_empty + 1;
   uint64_t* scale_full = final_bar + 1;  // [2]: tile scales ready (kFuse), by tile parity
-  uint32_t* tmem_slot = (uint32_t*)(scale_full + 2);
+  uint64_t* pfull = scale_full + 2;      // [2] kSplit: the peer's column maxima have landed
+  uint64_t* out_ready = pfull + 2;       // kSplit, rank 1: rank 0 has stored the tile
+  uint64_t* out_done = out_ready + 1;    // kSplit, rank 0: rank 1 has added its partial
+  uint32_t* tmem_slot = (uint32_t*)(out_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long n_tiles = (long long)p.tiles_m * p.tiles_n;
   const int nkc = (p.K + kKC - 1) / kKC;
+  const uint32_t rank = kSplit ? cluster_ctarank() : 0u;
+  const uint32_t peer = rank ^ 1u;
+  // tiles of this CTA (of this cluster when kSplit) and its k-chunk range
+  const long long w0 = kSplit ? blockIdx.x / 2 : blockIdx.x;
+  const long long wstep = kSplit ? gridDim.x / 2 : gridDim.x;
+  const int k_lo = kSplit && rank ? (nkc + 1) / 2 : 0;
+  const int k_hi = kSplit && !rank ? (nkc + 1) / 2 : nkc;
+  const int nkl = k_hi - k_lo;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFStages; ++s) {
@@ -115,6 +179,10 @@ static __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(final_bar, 1);
     mbar_init(&scale_full[0], 32);
     mbar_init(&scale_full[1], 32);
+    mbar_init(&pfull[0], 32);
+    mbar_init(&pfull[1], 32);
+    mbar_init(out_ready, 32 * kEpiWarps);
+    mbar_init(out_done, 32 * kEpiWarps);
     fence_mbar_init();
     tma_prefetch_desc(&mapA);
     tma_prefetch_desc(&mapX);
@@ -125,6 +193,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (kSplit) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -144,6 +213,9 @@ static __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* fill_bar = fp32 ? fullF : fullA;
       uint32_t it = 0;
       bool ok = true;
+#ifdef TT_OZC_PROFILE
+      long long w_prod = 0;
+#endif
       const uint64_t keep = l2_policy_evict_last(), drop = l2_policy_evict_first();
       // one ring slot: wait for it, then fill it with chunk kc of tile w
       // (max_pass: the first of the strip's two reads)
@@ -152,10 +224,16 @@ static __global__ void __launch_bounds__(kThreads, 1)
         int m0, n0;
         tile_of(w, m0, n0);
         const int s = it % nst;
+#ifdef TT_OZC_PROFILE
+        const long long tw = clock64();
+#endif
         if (!mbar_wait(&wait_bar[s], ((it / nst) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
           ok = false;
           return;
         }
+#ifdef TT_OZC_PROFILE
+        w_prod += clock64() - tw;
+#endif
         if (fp32) {
           mbar_arrive_expect_tx(&fill_bar[s], kFBytes);
           if (kFuse && p.l2hint)
@@ -172,11 +250,11 @@ static __global__ void __launch_bounds__(kThreads, 1)
       // fused scales: the fp32 stream is the first tile's strip (maxima), then
       // per tile the chunks of the next tile's strip (maxima) interleaved with
       // the current tile's (conversion), in the order the converters take them
-      if (kFuse && fp32 && blockIdx.x < n_tiles)
-        for (int kc = 0; kc < nkc; ++kc) issue(blockIdx.x, kc, true);
-      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x) {
-        const long long nxt = w + gridDim.x;
-        for (int kc = 0; kc < nkc; ++kc) {
+      if (kFuse && fp32 && w0 < n_tiles)
+        for (int kc = k_lo; kc < k_hi; ++kc) issue(w0, kc, true);
+      for (long long w = w0; w < n_tiles && ok; w += wstep) {
+        const long long nxt = w + wstep;
+        for (int kc = k_lo; kc < k_hi; ++kc) {
           issue(w, kc, false);
           if (kFuse && fp32 && nxt < n_tiles) issue(nxt, kc, true);
         }
@@ -184,6 +262,9 @@ static __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t issued = it;
       for (uint32_t k = (issued > (uint32_t)nst ? issued - nst : 0); k < issued; ++k)
         mbar_wait_drain(&fill_bar[k % nst], (k / nst) & 1u);
+#ifdef TT_OZC_PROFILE
+      if (p.prof) p.prof[blockIdx.x * 8 + (fp32 ? 6 : 7)] = w_prod;
+#endif
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
@@ -195,7 +276,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
       long long w_acc = 0, w_a = 0, w_c = 0;
       const long long t_begin = clock64();
 #endif
-      for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x, ++round) {
+      for (long long w = w0; w < n_tiles && ok; w += wstep, ++round) {
 #ifdef TT_OZC_PROFILE
         long long t0 = clock64();
 #endif
@@ -204,7 +285,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
         w_acc += clock64() - t0;
 #endif
         tc_fence_after();
-        for (int kc = 0; kc < nkc; ++kc, ++it) {
+        for (int kc = k_lo; kc < k_hi; ++kc, ++it) {
           const int s = it % kIStages;
           const uint32_t ph = (it / kIStages) & 1u;
 #ifdef TT_OZC_PROFILE
@@ -236,7 +317,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
               a[t] = smem_desc(sa + t * oz::kSliceTile + ks * 4096, 8192, 1024, 2);
               b[t] = smem_desc(sb + t * oz::kSliceTile + ks * 4096, 8192, 1024, 2);
             }
-            const uint32_t first = (kc | ks) != 0;
+            const uint32_t first = ((kc - k_lo) | ks) != 0;
             mma_i8_fill(tmem + 0 * kTile, a[0], b[0], idesc, first);
             mma_i8_use(tmem + 1 * kTile, a[0], b[1], idesc, first);
             mma_i8_lastuse(tmem + 2 * kTile, a[0], b[2], idesc, first);
@@ -263,12 +344,12 @@ static __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
     const int q = warp & 3;
-    const int half = ew >> 2;  // this warp's 64-column half
+    const int half = ew >> 2;  // this warp's block of kEpiCols columns
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
     uint32_t round = 0;
-    for (long long w = blockIdx.x; w < n_tiles; w += gridDim.x, ++round) {
+    for (long long w = w0; w < n_tiles; w += wstep, ++round) {
       int m0, n0;
       tile_of(w, m0, n0);
       // stage the tile's column scales while the MMAs run (kFuse: the
@@ -288,7 +369,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
       const int nn = p.N - n0 < kTile ? p.N - n0 : kTile;
       // combine this thread's 64 columns and park them as fp32
 #pragma unroll
-      for (int c = half * (kTile / 2); c < (half + 1) * (kTile / 2); c += 16) {
+      for (int c = half * kEpiCols; c < (half + 1) * kEpiCols; c += 16) {
         int l2[16], l3[16], l4[16];
         tmem_ld16i(lane_base + 0 * kTile + c, l2);
         tmem_ld16i(lane_base + 1 * kTile + c, l3);
@@ -302,12 +383,17 @@ static __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(acc_empty);  // levels drained: the next tile's MMAs may start
+      // kSplit, rank 1: add onto rank 0's stored partial, so wait for it
+      const bool adder = kSplit && rank == 1;
+      if (adder && !group_all<32 * kEpiWarps, 1>(
+                       mbar_wait_cluster(out_ready, round & 1u, p.err, kDevTimeoutAcc)))
+        break;
       // Eight rounds through the 16-column stage: the warps owning columns
       // [16h, 16h+16) copy them out of TMEM, then all eight warps store
       // 128 rows x 16 columns (4 lanes x float4 per row).
       for (int h = 0; h < kTile / kQCols; ++h) {
         const int c0 = h * kQCols;
-        if (half == c0 / (kTile / 2)) {
+        if (half == c0 / kEpiCols) {
           float v[16];
           tmem_ld16(lane_base + kColPark + c0, v);
           tmem_ld_wait();
@@ -326,21 +412,40 @@ static __global__ void __launch_bounds__(kThreads, 1)
           const float* srow = ostage + r * kQLd;
           if (vec && ncols >= kQCols) {
             const float4 v = reinterpret_cast<const float4*>(srow)[l4];
-            if (kFuse && p.l2hint)
+            if (adder)
+              red_add_v4(crow + 4 * l4, v);
+            else if (kFuse && !kSplit && p.l2hint)  // (kSplit: rank 1 adds to these lines)
               __stcs(reinterpret_cast<float4*>(crow) + l4, v);
             else
               reinterpret_cast<float4*>(crow)[l4] = v;
           } else {
-            for (int c = l4; c < ncols && c < kQCols; c += 4) crow[c] = srow[c];
+            for (int c = l4; c < ncols && c < kQCols; c += 4) {
+              if (adder)
+                atomicAdd(crow + c, srow[c]);
+              else
+                crow[c] = srow[c];
+            }
           }
         }
         group_sync<32 * kEpiWarps, 1>();  // stage free for the next round
+      }
+      if (kSplit) {
+        if (rank == 0) {
+          // Tell rank 1 that this tile is stored; first make sure rank 1 has
+          // taken the previous one, so that out_ready never runs two phases ahead.
+          bool ok0 = round == 0 ||
+                     mbar_wait_cluster(out_done, (round - 1) & 1u, p.err, kDevTimeoutAcc);
+          if (!group_all<32 * kEpiWarps, 1>(ok0)) break;
+          mbar_arrive_cluster(mapa(smem_u32(out_ready), peer));
+        } else {
+          mbar_arrive_cluster(mapa(smem_u32(out_done), peer));
+        }
       }
     }
   } else if (warp < kAWarp) {
     // ----------------------------------------------------------- converters
     const int cw = warp - (2 + kEpiWarps);
-    constexpr int kRows = kKC / kCvtWarps;  // 8 rows per warp and stage
+    constexpr int kRows = kKC / kCvtWarps;  // rows per warp and stage
     uint32_t itF = 0, itI = 0;  // fp32 ring and int8 ring positions
     bool ok = true;
 #ifdef TT_OZC_PROFILE
@@ -379,18 +484,38 @@ static __global__ void __launch_bounds__(kThreads, 1)
       }
       release_f();
     };
-    // Column maxima of all converter warps -> scales of the tile with parity
-    // `par`: inv for the converters, escale[par] + scale_full[par] for the
-    // epilogue. Every converter thread calls this (it holds named barriers).
-    auto finish_scales = [&](uint32_t par) -> bool {
+    // Column maxima of all converter warps (and, kSplit, of the peer CTA's
+    // half of K) -> scales of this CTA's tile number tr: inv for the
+    // converters, escale[tr & 1] + scale_full[tr & 1] for the epilogue. Every
+    // converter thread calls this (it holds named barriers).
+    auto finish_scales = [&](uint32_t tr) -> bool {
+      const uint32_t par = tr & 1u;
       reinterpret_cast<float4*>(cmax)[cw * 32 + lane] = make_float4(mx[0], mx[1], mx[2], mx[3]);
       if (!group_all<32 * kCvtWarps, kCvtBar>(ok)) return false;
+      float mm[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        float m = 0.f;
+        mm[k] = 0.f;
 #pragma unroll
-        for (int v = 0; v < kCvtWarps; ++v) m = fmaxf(m, cmax[v * kTile + 4 * lane + k]);
-        const float sc = ozd::scale_for_max(m);
+        for (int v = 0; v < kCvtWarps; ++v) mm[k] = fmaxf(mm[k], cmax[v * kTile + 4 * lane + k]);
+      }
+      if (kSplit) {
+        // Publish this half's maxima in the peer's pmax[par] and take the
+        // peer's. The peer overwrites pmax[par] only for tile tr + 2, after
+        // it has waited on pfull for tile tr + 1, which this CTA arrives on
+        // after the group_sync below, i.e. after every read of pmax[par].
+        if (cw == 0) {
+          st_cluster_v4(mapa(smem_u32(pmax + par * kTile + 4 * lane), peer), mm);
+          mbar_arrive_cluster(mapa(smem_u32(&pfull[par]), peer));
+        }
+        const bool got = mbar_wait_cluster(&pfull[par], (tr >> 1) & 1u, p.err, kDevTimeoutFull);
+        if (!group_all<32 * kCvtWarps, kCvtBar>(got)) return false;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mm[k] = fmaxf(mm[k], pmax[par * kTile + 4 * lane + k]);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float sc = ozd::scale_for_max(mm[k]);
         inv[k] = ozd::inv_scale(sc);
         if (cw == 0) escale[par * kTile + 4 * lane + k] = sc;
       }
@@ -402,16 +527,16 @@ static __global__ void __launch_bounds__(kThreads, 1)
     // (and writes the scales of tile r + 2 into escale[r & 1]) has waited for
     // an int8 slot that the MMA freed inside tile r + 1, so the epilogue has
     // already read escale[r & 1] and waited on scale_full[r & 1] for tile r.
-    if (kFuse && blockIdx.x < n_tiles) {
+    if (kFuse && w0 < n_tiles) {
       mx[0] = mx[1] = mx[2] = mx[3] = 0.f;
-      for (int kc = 0; kc < nkc; ++kc) max_chunk();
+      for (int kc = 0; kc < nkl; ++kc) max_chunk();
       if (!finish_scales(0)) ok = false;
     }
     uint32_t round = 0;
-    for (long long w = blockIdx.x; w < n_tiles && ok; w += gridDim.x, ++round) {
+    for (long long w = w0; w < n_tiles && ok; w += wstep, ++round) {
       int m0, n0;
       tile_of(w, m0, n0);
-      const bool next = kFuse && w + gridDim.x < n_tiles;
+      const bool next = kFuse && w + wstep < n_tiles;
       if (!kFuse) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -421,7 +546,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       mx[0] = mx[1] = mx[2] = mx[3] = 0.f;
-      for (int kc = 0; kc < nkc; ++kc) {
+      for (int kc = 0; kc < nkl; ++kc) {
         const int s = itI % kIStages;
         const uint32_t ph = (itI / kIStages) & 1u;
         ++itI;
@@ -466,7 +591,7 @@ static __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&conv[s]);
         if (next) max_chunk();  // the producer queued it right after this chunk
       }
-      if (next && !finish_scales((round + 1) & 1u)) ok = false;
+      if (next && !finish_scales(round + 1)) ok = false;
     }
 #ifdef TT_OZC_PROFILE
     if (p.prof && cw == 0 && lane == 0) {
@@ -478,10 +603,24 @@ static __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (kSplit) cluster_sync();  // no remote access to this CTA's shared memory is left
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+template <bool kFuse>
+static __global__ void __launch_bounds__(kThreads, 1)
+    gemm_cvt_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX,
+                    Params p) {
+  gemm_cvt_body<kFuse, false>(mapA, mapX, p);
+}
+
+static __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_cvt_split_kernel(const __grid_constant__ CUtensorMap mapA,
+                          const __grid_constant__ CUtensorMap mapX, Params p) {
+  gemm_cvt_body<true, true>(mapA, mapX, p);
 }
 
 }  // namespace ozc
