@@ -220,6 +220,15 @@ int tt_gemm_f32(const float* A, int a_kmajor, long long strideA, const float* B,
                 long long strideB, float* C, long long strideC, int M, int N, int K, int batch,
                 void* workspace, size_t workspace_bytes, int* dev_status, void* stream);
 
+/* Failure-detection check (no counterpart in the reference): one thread waits,
+ * through the same bounded mbarrier wait every kernel here uses, on a phase
+ * that nothing completes. After budget_cycles (at most the kernels' own
+ * budget, about 2 s) the wait gives up, *dev_status becomes 0x101 (a stage
+ * never arrived) and *dev_cycles the cycles waited; the context stays usable.
+ * Lets a caller test its handling of a device timeout without a GPU fault. */
+int tt_debug_wait_timeout(int* dev_status, long long budget_cycles, long long* dev_cycles,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -132,3 +132,35 @@ def test_nonfinite_eri_propagates(cuda_ok):
     keep = torch.ones(70, dtype=torch.bool)
     keep[9] = False
     assert torch.equal(out[:, :, keep], clean[:, :, keep])
+
+
+def test_device_wait_timeout_is_reported(cuda_ok):
+    """Failure detection without a GPU fault: a bounded device wait on an
+    mbarrier phase that nothing completes gives up after its budget, records
+    0x101 in the status word, and the context stays usable (the next energy
+    is still correct). The status word raises DeviceError on the host."""
+    import ctypes
+
+    from trntensor_b200 import _lib
+    from trntensor_b200.dispatch import _check_status
+
+    lib = _lib.load()
+    status = torch.full((), 7, dtype=torch.int32, device="cuda")
+    cycles = torch.zeros((), dtype=torch.int64, device="cuda")
+    budget = 20_000_000  # ~10 ms of SM clock
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.tt_debug_wait_timeout(ctypes.c_void_p(status.data_ptr()), budget,
+                                         ctypes.c_void_p(cycles.data_ptr()), stream),
+               "tt_debug_wait_timeout")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0x101
+    assert budget <= int(cycles.item()) < 50 * budget
+    with pytest.raises(_lib.DeviceError):
+        _check_status(status, "wait")
+    with pytest.raises(ValueError):
+        _lib.check(lib.tt_debug_wait_timeout(ctypes.c_void_p(status.data_ptr()), -1,
+                                             ctypes.c_void_p(cycles.data_ptr()), stream), "x")
+    B, eo, ev = mp2_inputs(3, 150, 40, seed=9)
+    ref, _ = oracle.mp2_energy_fp64(B.numpy(), eo.numpy(), ev.numpy())
+    e = tt.mp2_energy(B.cuda(), eo.cuda(), ev.cuda())
+    assert rel(e.item(), ref) <= 2e-6

@@ -1,5 +1,6 @@
 // Device checks, tensor-map encoding and status strings for the C ABI.
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace tt {
 
@@ -59,9 +60,34 @@ int encode_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* di
   return res == CUDA_SUCCESS ? TT_OK : TT_ERR_TMA;
 }
 
+// One thread waits, with the library's bounded mbarrier wait, on a phase
+// that nothing completes; the wait gives up after `budget` cycles and
+// records kDevTimeoutFull in *status, as every kernel's waits do.
+__global__ void wait_timeout_kernel(int* status, long long budget, long long* cycles) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  const long long t0 = clock64();
+  mbar_wait_budget(&bar, 0, status, kDevTimeoutFull, budget);
+  *cycles = clock64() - t0;
+}
+
 }  // namespace tt
 
 extern "C" {
+
+int tt_debug_wait_timeout(int* dev_status, long long budget_cycles, long long* dev_cycles,
+                          void* stream) {
+  if (!dev_status || !dev_cycles) return TT_ERR_NULL;
+  if (budget_cycles < 0 || budget_cycles > tt::kWaitBudgetCycles) return TT_ERR_SHAPE;
+  int st = tt::check_device(nullptr);
+  if (st != TT_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  TT_CUDA(cudaMemsetAsync(dev_status, 0, sizeof(int), s));
+  tt::wait_timeout_kernel<<<1, 32, 0, s>>>(dev_status, budget_cycles, dev_cycles);
+  return tt::cuda_status(cudaGetLastError());
+}
 
 const char* tt_status_string(int status) {
   switch (status) {

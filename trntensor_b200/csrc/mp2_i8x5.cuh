@@ -297,9 +297,9 @@ static __global__ void __launch_bounds__(kThreads, 1)
           arow ? (__ldg(P.eps_occ + t.i) + __ldg(P.eps_occ + t.j)) - __ldg(P.eps_vir + a) : 0.0;
       // sum of the (a,b) + (b,a) terms over 16 columns starting at c; x may
       // point into registers or into this thread's own scratch row
-      auto chunk_energy = [&](int c, const double* x, const double (&y)[16]) {
+      auto chunk_energy = [&](int c, const double* x, const double* y) {
         double part = 0.0;
-#pragma unroll
+#pragma unroll 4
         for (int k = 0; k < 16; ++k) {
           const int b = t.b0 + c + k;
           if (arow && b < p.nvir && a <= b) {
@@ -320,38 +320,36 @@ static __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      // Values are completed into the scratch tile and the accumulator is
+      // released before the fp64 energy terms are formed, so that the next
+      // sweep's MMAs do not wait for them.
+      auto finish_into = [&](double* dst, double srow, int occ_col) {
+        for (int c = c0; c < c0 + kBlk / 2; c += 16) {
+          double v[16];
+          sweep1_chunk(c, dst, srow, occ_col, t.b0, v);
+          double2* d2 = reinterpret_cast<double2*>(dst + row * kBlk + c);
+#pragma unroll
+          for (int k = 0; k < 16; k += 2) d2[k / 2] = make_double2(v[k], v[k + 1]);
+        }
+        tc_fence_before();
+        mbar_arrive(acc_empty);
+        ++round;
+      };
       if (t.i == t.j) {
         // T_ii symmetric: y = x
-        for (int c = c0; c < c0 + kBlk / 2; c += 16) {
-          double x[16];
-          sweep1_chunk(c, xs, sa_x, t.j, t.b0, x);
-          acc += chunk_energy(c, x, x);
-        }
-        tc_fence_before();
-        mbar_arrive(acc_empty);
-        ++round;
+        finish_into(xs, sa_x, t.j);
+        for (int c = c0; c < c0 + kBlk / 2; c += 16)
+          acc += chunk_energy(c, xs + row * kBlk + c, xs + row * kBlk + c);
       } else {
-        // complete x into the X tile
-        for (int c = c0; c < c0 + kBlk / 2; c += 16) {
-          double x[16];
-          sweep1_chunk(c, xs, sa_x, t.j, t.b0, x);
-          double2* d2 = reinterpret_cast<double2*>(xs + row * kBlk + c);
-#pragma unroll
-          for (int k = 0; k < 16; k += 2) d2[k / 2] = make_double2(x[k], x[k + 1]);
-        }
-        tc_fence_before();
-        mbar_arrive(acc_empty);
-        ++round;
+        finish_into(xs, sa_x, t.j);  // complete x into the X tile
         if (t.a0 == t.b0) {
           // diagonal block: y[a][b] = x[b][a], read back transposed from X
           group_sync<32 * kEpiWarps, 1>();
-          for (int c = c0; c < c0 + kBlk / 2; c += 16) {
-            double y[16];
-#pragma unroll
-            for (int k = 0; k < 16; ++k) y[k] = xs[(c + k) * kBlk + row];
-            acc += chunk_energy(c, xs + row * kBlk + c, y);
-          }
+          // (gathered into this thread's row of the Yp tile first)
+          for (int c = c0; c < c0 + kBlk / 2; ++c) yp[row * kBlk + c] = xs[c * kBlk + row];
           group_sync<32 * kEpiWarps, 1>();  // X free for the next item
+          for (int c = c0; c < c0 + kBlk / 2; c += 16)
+            acc += chunk_energy(c, xs + row * kBlk + c, yp + row * kBlk + c);
         } else {
           // ---- phase y: operands B_j[A], B_i[B]
           const double sa_y = arow ? __ldg(P.scale + (long long)t.j * p.nvir + a) : 0.0;
@@ -361,14 +359,9 @@ static __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          for (int c = c0; c < c0 + kBlk / 2; c += 16) {
-            double y[16];
-            sweep1_chunk(c, yp, sa_y, t.i, t.b0, y);
-            acc += chunk_energy(c, xs + row * kBlk + c, y);
-          }
-          tc_fence_before();
-          mbar_arrive(acc_empty);
-          ++round;
+          finish_into(yp, sa_y, t.i);
+          for (int c = c0; c < c0 + kBlk / 2; c += 16)
+            acc += chunk_energy(c, xs + row * kBlk + c, yp + row * kBlk + c);
         }
       }
       const double wgt = (t.i == t.j) ? 1.0 : 2.0;

@@ -55,7 +55,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on an mbarrier phase. Returns false (after recording `code`
 // in *err) when the budget runs out or when another thread already recorded
 // an error, so that every role of the kernel can unwind instead of hanging.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_budget(uint64_t* bar, uint32_t parity, int* err,
+                                                 int code, long long budget) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   uint32_t n = 0;
@@ -63,12 +64,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 1023u) == 0) {
       if (*(volatile int*)err != 0) return false;
-      if (clock64() - t0 > kWaitBudgetCycles) {
+      if (clock64() - t0 > budget) {
         atomicCAS(err, 0, code);
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_budget(bar, parity, err, code, kWaitBudgetCycles);
 }
 
 // Bounded wait used only on teardown paths: no error recording.
