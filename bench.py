@@ -401,7 +401,38 @@ def measure_ao2mo(args, rank, world, local):
         res["cpu_baseline"] = {"ms": t_cpu * 1e3, "cores": _blas_threads(), "kind": "port",
                                "sample": f"two-step einsum port on a {w}-wide aux slab (fp32), "
                                          f"extrapolated x{naux // w}"}
-    del slab, ws, out
+    del ws, out
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1:
+        # fp64 transform (precision="kahan"): five-digit int8 tensor-core path
+        # and the CUDA-core fp64 path, same inputs promoted to fp64
+        from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
+
+        s64, co64, cv64 = slab.double(), co.double(), cv.double()
+        del slab
+        torch.cuda.empty_cache()
+
+        def t64(kernel, n):
+            out64 = _cuda_ao_to_mo_transform(s64, co64, cv64, kernel=kernel)
+            torch.cuda.synchronize(dev)
+            a64, b64 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a64.record()
+            for _ in range(n):
+                out64 = _cuda_ao_to_mo_transform(s64, co64, cv64, kernel=kernel)
+            b64.record()
+            torch.cuda.synchronize(dev)
+            return a64.elapsed_time(b64) / n, out64
+
+        ms_tc, o_tc = t64("tc", 3)
+        ms_s, o_s = t64("simt", 1)
+        res["fp64"] = {"ms": ms_tc, "TFLOP_per_s": flops / ms_tc / 1e9,
+                       "kernel": "oz64::gemm_kernel (int8 tcgen05, 6-digit Ozaki, fp64 out)",
+                       "cuda_core_fp64_ms": ms_s,
+                       "max_rel_diff_tc_vs_cuda_core":
+                           float((o_tc - o_s).abs().max() / o_s.abs().max())}
+        del s64, o_tc, o_s
+    else:
+        del slab
     torch.cuda.empty_cache()
     return res
 

@@ -193,7 +193,22 @@ int tt_ao2mo_simt_f32(const float* eri, const float* C_occ, const float* C_vir, 
                       int nocc, int nvir, int naux, void* workspace, size_t workspace_bytes,
                       float* B_out, void* stream);
 
-/* The same in fp64 (precision="kahan" and float64 inputs). */
+/* Workspace of tt_ao2mo_f64_tc: six int8 digit planes of C_occ, C_vir, eri
+ * and the intermediate, fp64 column scales, and the fp64 intermediate. */
+size_t tt_ao2mo_f64_workspace_bytes(int nbf, int nocc, int nvir, int naux);
+
+/* AO->MO transform of fp64 inputs on int8 tensor cores (precision="kahan":
+ * trntensor/einsum.py:108-111 applied to the two-step form of
+ * trntensor/quantum.py:188-194; replaces the fp64 route through
+ * trntensor/nki/dispatch.py:286-336): six-digit column-scaled Ozaki split,
+ * 21 exact int8 GEMMs per tile, fp64 output; max|dB|/max|B| ~ 1e-14.
+ * nbf <= 26214 (TT_ERR_SHAPE otherwise). dev_status as for tt_ao2mo_f32. */
+int tt_ao2mo_f64_tc(const double* eri, const double* C_occ, const double* C_vir, int nbf,
+                    int nocc, int nvir, int naux, void* workspace, size_t workspace_bytes,
+                    double* B_out, int* dev_status, void* stream);
+
+/* The same in fp64 on CUDA cores (precision="kahan" and float64 inputs):
+ * the path for nbf beyond tt_ao2mo_f64_tc's limit, and its cross-check. */
 int tt_ao2mo_f64(const double* eri, const double* C_occ, const double* C_vir, int nbf,
                  int nocc, int nvir, int naux, void* workspace, size_t workspace_bytes,
                  double* B_out, void* stream);

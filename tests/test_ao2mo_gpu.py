@@ -200,3 +200,26 @@ def test_step1_fused_scales_match_column_pass(cuda_ok, shape, monkeypatch):
     assert max_rel(fused.cpu().numpy(), ref) <= TOL_F32
     if nbf <= 320:
         assert torch.equal(split, fused)
+
+
+@pytest.mark.parametrize("shape", [(200, 10, 20, 24), (128, 16, 112, 384), (300, 130, 70, 50),
+                                   (1024, 128, 96, 160), (33, 1, 2, 3)])
+def test_fp64_tensor_core_vs_cuda_core(cuda_ok, shape):
+    """fp64 transform (precision="kahan"): the five-digit int8 tensor-core path
+    and the CUDA-core fp64 path agree to the fp64 tolerance (ragged tiles in
+    every dimension, columns of very different magnitude)."""
+    from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
+
+    nbf, nocc, nvir, naux = shape
+    g = torch.Generator().manual_seed(nbf * 7 + naux)
+    eri = torch.randn(nbf, nbf, naux, generator=g, dtype=torch.float64)
+    eri *= torch.logspace(-4, 4, naux, dtype=torch.float64)
+    co = torch.randn(nbf, nocc, generator=g, dtype=torch.float64)
+    cv = torch.randn(nbf, nvir, generator=g, dtype=torch.float64)
+    tc = _cuda_ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda())
+    simt = _cuda_ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda(), kernel="simt")
+    assert tc.dtype == torch.float64
+    assert max_rel(tc.cpu().numpy(), simt.cpu().numpy()) <= TOL_F64
+    # per aux column as well: each column has its own scale
+    col = (tc - simt).abs().amax(dim=(0, 1)) / simt.abs().amax(dim=(0, 1))
+    assert float(col.max()) <= 1e-11

@@ -126,12 +126,18 @@ def test_nonfinite_eri_propagates(cuda_ok):
 
     eri, co, cv = ao2mo_inputs(130, 5, 20, 70, seed=3)
     clean = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda()).cpu()
+    clean64 = tt.ao_to_mo_transform(eri.double().cuda(), co.double().cuda(),
+                                    cv.double().cuda()).cpu()
     eri[17, 40, 9] = float("inf")
     out = tt.ao_to_mo_transform(eri.cuda(), co.cuda(), cv.cuda()).cpu()
     assert not torch.isfinite(out[:, :, 9]).all()
     keep = torch.ones(70, dtype=torch.bool)
     keep[9] = False
     assert torch.equal(out[:, :, keep], clean[:, :, keep])
+    out64 = tt.ao_to_mo_transform(eri.double().cuda(), co.double().cuda(),
+                                  cv.double().cuda()).cpu()
+    assert not torch.isfinite(out64[:, :, 9]).all()
+    assert torch.equal(out64[:, :, keep], clean64[:, :, keep])
 
 
 def test_device_wait_timeout_is_reported(cuda_ok):

@@ -3,6 +3,7 @@
 #include "common.cuh"
 #include "ozaki_gemm.cuh"
 #include "ozaki_gemm_cvt.cuh"
+#include "ozaki_gemm64.cuh"
 
 #include <cstdlib>
 
@@ -47,6 +48,9 @@ int setup(int dev) {
         return TT_ERR_CUDA;
       g_split_clusters[dev] = n;
     }
+    if (cudaFuncSetAttribute(oz64::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             oz64::kSmemBytes) != cudaSuccess)
+      return TT_ERR_CUDA;
     if (cudaFuncSetAttribute(oz::gemm_kernel<false, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              oz::kSmemBytes) != cudaSuccess)
@@ -120,6 +124,77 @@ int oz_gemm(const int8_t* QA, const float* SA, int mpad, int batchA, const int8_
   const long long tiles = (long long)p.tiles_m * p.tiles_n * batch;
   const int grid = (int)(tiles < sms ? tiles : sms);
   oz::gemm_kernel<false, false><<<grid, oz::kThreads, oz::kSmemBytes, s>>>(ma, mb, p);
+  return cuda_status(cudaGetLastError());
+}
+
+// fp64 tensor-core workspace: six digit planes per operand, fp64 scales.
+struct OzLayout64 {
+  size_t qo, so, qv, sv, qe, se, inter, qi, si, total;
+  OzLayout64(size_t nbf, size_t nocc, size_t nvir, size_t naux) {
+    size_t o = 0;
+    auto take = [&o](size_t bytes) { size_t r = o; o += al256(bytes); return r; };
+    constexpr size_t D = oz64::kDigits;
+    qo = take(D * nbf * pad16(nocc));
+    so = take(8 * pad16(nocc));
+    qv = take(D * nbf * pad16(nvir));
+    sv = take(8 * pad16(nvir));
+    qe = take(D * nbf * pad16(nbf * naux));
+    se = take(8 * pad16(nbf * naux));
+    inter = take(8 * nocc * nbf * naux);
+    qi = take(D * nocc * nbf * pad16(naux));
+    si = take(8 * nocc * pad16(naux));
+    total = o;
+  }
+};
+
+int split_cols64(const double* X, long long ldx, long long bsx, int batch, int K, int N, int npad,
+                 int8_t* Q, double* S, cudaStream_t s, int sms) {
+  const long long nblk = (long long)batch * ((npad + oz64::kSplitCols - 1) / oz64::kSplitCols);
+  const long long cap = (long long)sms * 8;
+  const int grid = (int)(nblk < cap ? nblk : cap);
+  oz64::colmax_kernel<<<grid, oz64::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S);
+  oz64::slice_kernel<<<grid, oz64::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S, Q);
+  return cuda_status(cudaGetLastError());
+}
+
+// Tensor map over digit planes Q[6][batch][K][npad], box 128 x 32 x 1 x nd.
+int slice_map64(CUtensorMap* m, const int8_t* Q, int npad, int K, int batch, int nd) {
+  const uint64_t dims[4] = {(uint64_t)npad, (uint64_t)K, (uint64_t)batch,
+                            (uint64_t)oz64::kDigits};
+  const uint64_t strides[3] = {(uint64_t)npad, (uint64_t)npad * K, (uint64_t)npad * K * batch};
+  const uint32_t box[4] = {(uint32_t)oz64::kTile, (uint32_t)oz64::kKC, 1, (uint32_t)nd};
+  return encode_tmap(m, Q, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_DATA_TYPE_UINT8);
+}
+
+int oz_gemm64(const int8_t* QA, const double* SA, int mpad, int batchA, const int8_t* QB,
+              const double* SB, int npad, int batch, int M, int N, int K, double* C,
+              long long ldc, long long strideC, int* err, cudaStream_t s, int sms) {
+  CUtensorMap a3, a5, b3, b5;
+  if (slice_map64(&a3, QA, mpad, K, batchA, 3) ||
+      slice_map64(&a5, QA, mpad, K, batchA, oz64::kDigits) ||
+      slice_map64(&b3, QB, npad, K, batch, 3) ||
+      slice_map64(&b5, QB, npad, K, batch, oz64::kDigits))
+    return TT_ERR_TMA;
+  oz64::Params p;
+  p.sA = SA;
+  p.sB = SB;
+  p.ldsA = mpad;
+  p.ldsB = npad;
+  p.C = C;
+  p.ldc = ldc;
+  p.strideC = strideC;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.batch = batch;
+  p.shared_A = batchA == 1 && batch > 1;
+  p.tiles_m = (M + oz64::kTile - 1) / oz64::kTile;
+  p.tiles_n = (N + oz64::kTile - 1) / oz64::kTile;
+  p.err = err;
+  const long long tiles = (long long)p.tiles_m * p.tiles_n * batch;
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  oz64::gemm_kernel<<<grid, oz64::kThreads, oz64::kSmemBytes, s>>>(a3, a5, b3, b5, p);
   return cuda_status(cudaGetLastError());
 }
 
@@ -283,6 +358,58 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
   // step 2: B_out[i][a][P] = sum_n C_vir[n][a] inter[i][n][P]
   return oz_gemm(qv, sv, pv, 1, qi, si, pa, nocc, nvir, naux, nbf, B_out, naux,
                  (long long)nvir * naux, dev_status, s, sms);
+}
+
+size_t tt_ao2mo_f64_workspace_bytes(int nbf, int nocc, int nvir, int naux) {
+  if (nbf <= 0 || nocc <= 0 || nvir <= 0 || naux <= 0) return 0;
+  return tt::OzLayout64(nbf, nocc, nvir, naux).total;
+}
+
+int tt_ao2mo_f64_tc(const double* eri, const double* C_occ, const double* C_vir, int nbf,
+                    int nocc, int nvir, int naux, void* workspace, size_t workspace_bytes,
+                    double* B_out, int* dev_status, void* stream) {
+  using namespace tt;
+  if (!eri || !C_occ || !C_vir || !workspace || !B_out || !dev_status) return TT_ERR_NULL;
+  if (nbf <= 0 || nocc <= 0 || nvir <= 0 || naux <= 0) return TT_ERR_SHAPE;
+  if ((long long)nbf * naux > 0x7fffffffLL) return TT_ERR_SHAPE;
+  if (nbf > oz64::kMaxK) return TT_ERR_SHAPE;  // int32 digit sums exact up to this K
+  const OzLayout64 L(nbf, nocc, nvir, naux);
+  if (workspace_bytes < L.total) return TT_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return TT_ERR_ALIGN;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = setup(dev);
+  if (st != TT_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  TT_CUDA(cudaMemsetAsync(dev_status, 0, sizeof(int), s));
+  char* w = static_cast<char*>(workspace);
+  int8_t* qo = (int8_t*)(w + L.qo);
+  double* so = (double*)(w + L.so);
+  int8_t* qv = (int8_t*)(w + L.qv);
+  double* sv = (double*)(w + L.sv);
+  int8_t* qe = (int8_t*)(w + L.qe);
+  double* se = (double*)(w + L.se);
+  double* inter = (double*)(w + L.inter);
+  int8_t* qi = (int8_t*)(w + L.qi);
+  double* si = (double*)(w + L.si);
+  const int sms = g_sms[dev];
+  const int po = (int)pad16(nocc), pv = (int)pad16(nvir), pe = (int)pad16((size_t)nbf * naux),
+            pa = (int)pad16(naux);
+  const long long ncol = (long long)nbf * naux;
+  if ((st = split_cols64(C_occ, nocc, 0, 1, nbf, nocc, po, qo, so, s, sms))) return st;
+  if ((st = split_cols64(C_vir, nvir, 0, 1, nbf, nvir, pv, qv, sv, s, sms))) return st;
+  if ((st = split_cols64(eri, ncol, 0, 1, nbf, nbf * naux, pe, qe, se, s, sms))) return st;
+  // step 1: inter[i][(n,P)] = sum_m C_occ[m][i] eri[m][(n,P)]
+  if ((st = oz_gemm64(qo, so, po, 1, qe, se, pe, 1, nocc, nbf * naux, nbf, inter, ncol, 0,
+                      dev_status, s, sms)))
+    return st;
+  // digits of inter[i] (K = n, N = P), scales per (i, P)
+  if ((st = split_cols64(inter, naux, (long long)nbf * naux, nocc, nbf, naux, pa, qi, si, s, sms)))
+    return st;
+  // step 2: B_out[i][a][P] = sum_n C_vir[n][a] inter[i][n][P]
+  return oz_gemm64(qv, sv, pv, 1, qi, si, pa, nocc, nvir, naux, nbf, B_out, naux,
+                   (long long)nvir * naux, dev_status, s, sms);
 }
 
 int tt_ao2mo_simt_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf, int nocc,

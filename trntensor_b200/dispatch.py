@@ -209,6 +209,8 @@ def _cuda_mp2_energy(
 OZAKI_MAX_K = 65535
 # The five-digit fp64 kernel (csrc/mp2_i8x5.cuh): K * (2*64*128 + 3*128*128) < 2^31.
 OZAKI_F64_MAX_K = 32767
+# The six-digit fp64 GEMM (csrc/ozaki_gemm64.cuh): K * (2*64*128 + 4*128*128) < 2^31.
+OZAKI_GEMM_F64_MAX_K = 26214
 
 
 def pair_offset(i: int, nocc: int) -> int:
@@ -302,8 +304,8 @@ def _cuda_ao_to_mo_transform(
 ) -> torch.Tensor:
     """AO->MO transform on the current CUDA device; result stays on the device.
 
-    ``kernel="tc"``: int8 Ozaki tensor cores (fp32 product path);
-    ``kernel="simt"``: plain fp32 CUDA-core cross-check.
+    ``kernel="tc"``: int8 Ozaki tensor cores (three digits for fp32, six for
+    fp64); ``kernel="simt"``: plain CUDA-core cross-check in the same precision.
 
     fp32 inputs compute in fp32, float64 inputs or ``precision="kahan"`` in
     fp64 (trntensor/einsum.py:108-111 semantics: the caller casts back).
@@ -321,6 +323,16 @@ def _cuda_ao_to_mo_transform(
     e = _to_dev(eri, dev, cdt)
     co = _to_dev(C_occ, dev, cdt)
     cv = _to_dev(C_vir, dev, cdt)
+    if cdt == torch.float64 and kernel == "tc" and nbf <= OZAKI_GEMM_F64_MAX_K:
+        ws_bytes = int(lib.tt_ao2mo_f64_workspace_bytes(nbf, nocc, nvir, naux))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        dev_status = torch.empty((), dtype=torch.int32, device=dev)
+        st = lib.tt_ao2mo_f64_tc(_ptr(e), _ptr(co), _ptr(cv), nbf, nocc, nvir, naux, _ptr(ws),
+                                 ws_bytes, _ptr(out), _ptr(dev_status),
+                                 ctypes.c_void_p(_stream_handle()))
+        _lib.check(st, "tt_ao2mo_f64_tc")
+        _check_status(dev_status, "tt_ao2mo_f64_tc")
+        return out
     esz = 8 if cdt == torch.float64 else 4
     ws_bytes = int(lib.tt_ao2mo_workspace_bytes(nbf, nocc, nvir, naux, esz))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
