@@ -50,10 +50,14 @@ namespace mp2d {
 constexpr int kBlk = 128;
 constexpr int kKC = 32;                        // aux elements (bytes) per stage = one k-step
 constexpr int kDigits = 5;
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kSliceTile = kBlk * kKC;         // 4 KB, 32B swizzle
-constexpr int kOperandBytes = kDigits * kSliceTile;  // 20 KB
-constexpr int kStageBytes = 2 * kOperandBytes;       // A and B: 40 KB
+// A stage holds two k-steps of sweep 0 (3 digits each) or one of sweep 1
+// (5 digits): A at offset 0, B at kOperandBytes, k-step 1 of sweep 0 at
+// +3 slices. Sweep 0 then has as much MMA work per stage as sweep 1, so
+// that the same ring depth covers the load latency in both sweeps.
+constexpr int kOperandBytes = 6 * kSliceTile;  // 24 KB
+constexpr int kStageBytes = 2 * kOperandBytes; // 48 KB
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
@@ -138,8 +142,9 @@ static __global__ void __launch_bounds__(kThreads, 1)
           const int occA = r < 2 ? t.i : t.j;
           const int occB = r < 2 ? t.j : t.i;
           const CUtensorMap* map = sweep ? &map5 : &map3;
-          const uint32_t bytes = 2u * sweep_digits(sweep) * kSliceTile;
-          for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int ksteps = sweep ? 1 : 2;  // k-steps per stage
+          const uint32_t bytes = 2u * ksteps * sweep_digits(sweep) * kSliceTile;
+          for (int kc = 0; kc < nkc; kc += ksteps, ++it) {
             const int s = it % kStages;
             if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
               ok = false;
@@ -147,8 +152,11 @@ static __global__ void __launch_bounds__(kThreads, 1)
             }
             uint8_t* st = smem + s * kStageBytes;
             mbar_arrive_expect_tx(&full[s], bytes);
-            tma_load_4d(st, map, &full[s], kc * kKC, t.a0, occA, 0);
-            tma_load_4d(st + kOperandBytes, map, &full[s], kc * kKC, t.b0, occB, 0);
+            for (int ks = 0; ks < ksteps; ++ks) {
+              const int off = ks * 3 * kSliceTile;
+              tma_load_4d(st + off, map, &full[s], (kc + ks) * kKC, t.a0, occA, 0);
+              tma_load_4d(st + kOperandBytes + off, map, &full[s], (kc + ks) * kKC, t.b0, occB, 0);
+            }
           }
         }
       }
@@ -171,7 +179,8 @@ static __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int ksteps = sweep ? 1 : 2;
+          for (int kc = 0; kc < nkc; kc += ksteps, ++it) {
             const int s = it % kStages;
             if (!mbar_wait(&full[s], (it / kStages) & 1u, p.err, kDevTimeoutFull)) {
               ok = false;
@@ -180,24 +189,34 @@ static __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t sa = smem_u32(smem + s * kStageBytes);
             const uint32_t sb = sa + kOperandBytes;
-            uint64_t a[kDigits], b[kDigits];
-#pragma unroll
-            for (int d = 0; d < kDigits; ++d) {
-              a[d] = smem_desc(sa + d * kSliceTile, 16, 256, 6);
-              b[d] = smem_desc(sb + d * kSliceTile, 16, 256, 6);
-            }
-            const uint32_t acc = kc != 0;
             // Grouped by A digit (collector buffer: each A digit is read from
             // shared memory once per k-step). Level l sits at column 128 l
             // (sweep 0: L0..L2) or 128 (l - 3) (sweep 1: L3..L5).
             if (sweep == 0) {
-              mma_i8_fill(tmem + 0 * kBlk, a[0], b[0], idesc, acc);
-              mma_i8_use(tmem + 1 * kBlk, a[0], b[1], idesc, acc);
-              mma_i8_lastuse(tmem + 2 * kBlk, a[0], b[2], idesc, acc);
-              mma_i8_fill(tmem + 1 * kBlk, a[1], b[0], idesc, 1);
-              mma_i8_lastuse(tmem + 2 * kBlk, a[1], b[1], idesc, 1);
-              mma_i8(tmem + 2 * kBlk, a[2], b[0], idesc, 1);
+#pragma unroll
+              for (int ks = 0; ks < 2; ++ks) {
+                uint64_t a[3], b[3];
+#pragma unroll
+                for (int d = 0; d < 3; ++d) {
+                  a[d] = smem_desc(sa + (3 * ks + d) * kSliceTile, 16, 256, 6);
+                  b[d] = smem_desc(sb + (3 * ks + d) * kSliceTile, 16, 256, 6);
+                }
+                const uint32_t acc = (kc | ks) != 0;
+                mma_i8_fill(tmem + 0 * kBlk, a[0], b[0], idesc, acc);
+                mma_i8_use(tmem + 1 * kBlk, a[0], b[1], idesc, acc);
+                mma_i8_lastuse(tmem + 2 * kBlk, a[0], b[2], idesc, acc);
+                mma_i8_fill(tmem + 1 * kBlk, a[1], b[0], idesc, 1);
+                mma_i8_lastuse(tmem + 2 * kBlk, a[1], b[1], idesc, 1);
+                mma_i8(tmem + 2 * kBlk, a[2], b[0], idesc, 1);
+              }
             } else {
+              uint64_t a[kDigits], b[kDigits];
+#pragma unroll
+              for (int d = 0; d < kDigits; ++d) {
+                a[d] = smem_desc(sa + d * kSliceTile, 16, 256, 6);
+                b[d] = smem_desc(sb + d * kSliceTile, 16, 256, 6);
+              }
+              const uint32_t acc = kc != 0;
               mma_i8_fill(tmem + 0 * kBlk, a[0], b[3], idesc, acc);
               mma_i8_lastuse(tmem + 1 * kBlk, a[0], b[4], idesc, acc);
               mma_i8_fill(tmem + 0 * kBlk, a[1], b[2], idesc, 1);

@@ -19,7 +19,9 @@
 // adds sweep 1's levels to it (each thread re-reads only what it wrote).
 //
 // Tile M = N = 128 (MN-major, 128B swizzle: the layout of ozaki_gemm.cuh),
-// 32 k per stage, 4 stages of six digits of A and B.
+// 4 stages of 48 KB: one 32-wide k-step of six digits of A and B (sweep 1)
+// or two k-steps of three digits (sweep 0, k-step 1 at +3 slices), so both
+// sweeps give the ring the same MMA work per stage.
 // Roles: warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue.
 #pragma once
 #include "ozaki_digits.cuh"
@@ -118,17 +120,21 @@ static __global__ void __launch_bounds__(kThreads, 1)
         for (int sweep = 0; sweep < 2 && ok; ++sweep) {
           const CUtensorMap* ma = sweep ? &a5 : &a3;
           const CUtensorMap* mb = sweep ? &b5 : &b3;
-          const uint32_t bytes = 2u * sweep_digits(sweep) * kSliceTile;
-          for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int ksteps = sweep ? 1 : 2;  // k-steps per stage
+          for (int kc = 0; kc < nkc; kc += ksteps, ++it) {
             const int s = it % kStages;
             if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) {
               ok = false;
               break;
             }
             uint8_t* st = smem + s * kStageBytes;
-            mbar_arrive_expect_tx(&full[s], bytes);
-            tma_load_4d(st, ma, &full[s], t.m0, kc * kKC, bA, 0);
-            tma_load_4d(st + kOperandBytes, mb, &full[s], t.n0, kc * kKC, t.b, 0);
+            const int nks = kc + ksteps <= nkc ? ksteps : nkc - kc;
+            mbar_arrive_expect_tx(&full[s], 2u * nks * sweep_digits(sweep) * kSliceTile);
+            for (int ks = 0; ks < nks; ++ks) {
+              const int off = ks * 3 * kSliceTile;
+              tma_load_4d(st + off, ma, &full[s], t.m0, (kc + ks) * kKC, bA, 0);
+              tma_load_4d(st + kOperandBytes + off, mb, &full[s], t.n0, (kc + ks) * kKC, t.b, 0);
+            }
           }
         }
       }
@@ -148,7 +154,8 @@ static __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int ksteps = sweep ? 1 : 2;
+          for (int kc = 0; kc < nkc; kc += ksteps, ++it) {
             const int s = it % kStages;
             if (!mbar_wait(&full[s], (it / kStages) & 1u, p.err, kDevTimeoutFull)) {
               ok = false;
@@ -158,21 +165,31 @@ static __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t sa = smem_u32(smem + s * kStageBytes);
             const uint32_t sb = sa + kOperandBytes;
             // MN-major SW128: 8 k-rows of 128 B per 1 KB atom, 32 k = 4 atoms
-            uint64_t a[kDigits], b[kDigits];
-#pragma unroll
-            for (int d = 0; d < kDigits; ++d) {
-              a[d] = smem_desc(sa + d * kSliceTile, 8192, 1024, 2);
-              b[d] = smem_desc(sb + d * kSliceTile, 8192, 1024, 2);
-            }
-            const uint32_t acc = kc != 0;
             if (sweep == 0) {
-              mma_i8_fill(tmem + 0 * kTile, a[0], b[0], idesc, acc);
-              mma_i8_use(tmem + 1 * kTile, a[0], b[1], idesc, acc);
-              mma_i8_lastuse(tmem + 2 * kTile, a[0], b[2], idesc, acc);
-              mma_i8_fill(tmem + 1 * kTile, a[1], b[0], idesc, 1);
-              mma_i8_lastuse(tmem + 2 * kTile, a[1], b[1], idesc, 1);
-              mma_i8(tmem + 2 * kTile, a[2], b[0], idesc, 1);
+              const int nks = kc + 2 <= nkc ? 2 : nkc - kc;
+              for (int ks = 0; ks < nks; ++ks) {
+                uint64_t a[3], b[3];
+#pragma unroll
+                for (int d = 0; d < 3; ++d) {
+                  a[d] = smem_desc(sa + (3 * ks + d) * kSliceTile, 8192, 1024, 2);
+                  b[d] = smem_desc(sb + (3 * ks + d) * kSliceTile, 8192, 1024, 2);
+                }
+                const uint32_t acc = (kc | ks) != 0;
+                mma_i8_fill(tmem + 0 * kTile, a[0], b[0], idesc, acc);
+                mma_i8_use(tmem + 1 * kTile, a[0], b[1], idesc, acc);
+                mma_i8_lastuse(tmem + 2 * kTile, a[0], b[2], idesc, acc);
+                mma_i8_fill(tmem + 1 * kTile, a[1], b[0], idesc, 1);
+                mma_i8_lastuse(tmem + 2 * kTile, a[1], b[1], idesc, 1);
+                mma_i8(tmem + 2 * kTile, a[2], b[0], idesc, 1);
+              }
             } else {
+              uint64_t a[kDigits], b[kDigits];
+#pragma unroll
+              for (int d = 0; d < kDigits; ++d) {
+                a[d] = smem_desc(sa + d * kSliceTile, 8192, 1024, 2);
+                b[d] = smem_desc(sb + d * kSliceTile, 8192, 1024, 2);
+              }
+              const uint32_t acc = kc != 0;
               // L3 at column 0, L4 at 128, L5 at 256
               mma_i8_fill(tmem + 0 * kTile, a[0], b[3], idesc, acc);
               mma_i8_use(tmem + 1 * kTile, a[0], b[4], idesc, acc);
