@@ -440,7 +440,7 @@ def measure_ao2mo(args, rank, world, local):
 def run_ours(args, rank, world, local):
     import trntensor_b200 as tt
     from trntensor_b200 import _lib, distributed
-    from trntensor_b200.dispatch import _cuda_mp2_energy, pair_offset
+    from trntensor_b200.dispatch import _cuda_mp2_energy, first_row_of_pair, pair_offset
     from trntensor_b200.inputs import mp2_inputs
 
     lib = _lib.load()
@@ -598,7 +598,13 @@ def run_ours(args, rank, world, local):
     # end-to-end: public API, host (pinned) inputs, result back on the host
     e2e = None
     if not args.no_e2e:
-        Bh = B.cpu().pin_memory()
+        # Host copy of B in pinned memory, written straight from the device
+        # (no pageable staging copy: at N ranks that would hold N x 11.3 GB of
+        # host memory twice). The call reads only rows first_row(pb).. of it,
+        # so a rank fills those; the rest of the buffer stays unwritten.
+        i0 = first_row_of_pair(pb, nocc) if pe > pb else nocc
+        Bh = torch.empty(B.shape, dtype=B.dtype, pin_memory=True)
+        Bh[i0:].copy_(B[i0:])
         q = None  # slices no longer needed; the API allocates its own workspace
         torch.cuda.empty_cache()
         eoh, evh = eo.cpu(), ev.cpu()
