@@ -165,7 +165,7 @@ def test_step1_on_chip_split_matches_preslice(cuda_ok, shape, monkeypatch):
 
 
 @pytest.mark.parametrize("shape", [(256, 130, 100, 64), (520, 16, 40, 200), (1024, 128, 96, 160),
-                                   (390, 20, 30, 36)])
+                                   (390, 20, 30, 36), (400, 150, 40, 48), (400, 8, 8, 4)])
 def test_step1_fused_scales_match_column_pass(cuda_ok, shape, monkeypatch):
     """Step 1 computes eri's column scales inside the GEMM (a max pass over the
     next tile's strip while the current tile converts). With one CTA per tile
@@ -173,9 +173,9 @@ def test_step1_fused_scales_match_column_pass(cuda_ok, shape, monkeypatch):
     separate column-max pass (TRNTENSOR_B200_AO2MO_COLMAX=1): bit-identical
     tensors. The default for nbf > 320 splits K over a CTA pair (column maxima
     exchanged between the pair, rank 1 adding its partial onto rank 0's):
-    deterministic, and within the fp32 tolerance of fp64. nocc = 130 gives two
-    row tiles per strip, nbf = 520 and 390 ragged k halves, the 1024 case more
-    tiles than CTA pairs."""
+    deterministic, and within the fp32 tolerance of fp64. nocc = 130 and 150
+    give two row tiles per strip (the latter split-K), nbf = 520 and 390
+    ragged k halves, the 1024 case more tiles than CTA pairs, the last fewer."""
     from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
 
     nbf, nocc, nvir, naux = shape
