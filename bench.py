@@ -578,7 +578,9 @@ def run_ours(args, rank, world, local):
         "peak": peak_eff,
         "unit": "TFLOP/s",
         "frac": achieved / peak_eff,
-        "traffic": TRAFFIC_BYTES_PER_PAIR * my_pairs / max(1, energy_launches),
+        # measured at config 4's row length only; other configs report none
+        "traffic": (TRAFFIC_BYTES_PER_PAIR * my_pairs / max(1, energy_launches)
+                    if (nvir, naux) == (1792, 6144) else None),
         "kernel": "tt::mp2::energy_kernel",
         "launches_per_step": energy_launches,
         "kernel_ms": kernel_s * 1e3 / max(1, energy_launches),
@@ -666,7 +668,10 @@ def run_ours(args, rank, world, local):
             "data": "synthetic (seeded on device, BASELINE config distributions)",
             "config": {"workload": f"mp2_config{args.config}", "nocc": nocc, "nvir": nvir,
                        "naux": naux, "unique_pairs": npairs, "flops_per_step": job_flops,
-                       "l2": "inputs larger than L2 (B 11.3 GB fp32, slices 8.5 GB)",
+                       "l2": (f"B {nocc * nvir * naux * 4 / 1e9:.3g} GB fp32, slices "
+                             f"{nocc * nvir * naux * 3 / 1e9:.3g} GB: "
+                             + ("inputs larger than L2" if nocc * nvir * naux * 3 > 126e6
+                                else "inputs fit in L2 (not a bench line; parity size)")),
                        "parallelism": f"pairs sharded over {world} GPU(s), B replicated, "
                                       f"fp64 all-reduce"},
             "energy": energy_value,

@@ -1,0 +1,328 @@
+"""The int8 Ozaki digit formats of the device kernels, emulated exactly on CPU.
+
+The sm_100a kernels never multiply fp32 or fp64 values on the tensor cores:
+they split every operand row (MP2) or column (AO->MO, einsum GEMM) into int8
+digits with a power-of-two scale, run exact int8 x int8 -> int32 GEMMs and
+recombine the levels in the epilogue. These tests restate that arithmetic in
+numpy, bit for bit where the device code is bit-defined (scales, the
+magic-number rounding, byte permutes, digit bytes, int32 level sums), and check
+the properties the kernels rely on:
+
+* the digits reconstruct the input to the stated bound and stay in range;
+* the packed 32-bit words of ``ozd::pack_digits`` hold the right bytes;
+* the int32 level sums cannot overflow up to the contraction lengths that the
+  C ABI accepts (``ozd::kMaxK``, ``mp2d``/``oz64`` limits);
+* the energies and transformed tensors computed this way meet the tolerances
+  of the parity tests against the reference's golden vectors (|dE|/|E| <= 1e-6
+  fp32, 1e-12 fp64; max|dB| <= 1e-5 / 1e-12 of max|B|).
+
+A failure here means the format, not a kernel, is wrong; a GPU parity failure
+with these green points at the kernel.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from tests.helpers import AO_CASES, MP2_CASES, ao_case_inputs, mp2_case_inputs
+
+F32_MAX = np.float32(3.4028234e38)
+MAGIC = np.float32(12582912.0)  # 1.5 * 2^23
+MAGIC_BITS = 0x4B400000
+BIAS = 128 + 128 * 256
+
+
+# ---------------------------------------------------------------- fp32 digits
+# (csrc/ozaki_digits.cuh: scale_for_max, inv_scale, digit_word, pack_digits)
+
+def scale_for_max(mx: np.ndarray) -> np.ndarray:
+    """s = 2^(ilogb(mx) + 1 - 6); 0 for mx <= 1e-30; NaN for non-finite mx."""
+    mx = np.asarray(mx, dtype=np.float32)
+    _, ex = np.frexp(mx)  # mx = f 2^ex, f in [0.5, 1): ilogb = ex - 1
+    s = np.ldexp(np.float32(1.0), (ex - 6).astype(np.int32)).astype(np.float32)
+    s = np.where(mx > np.float32(1.0e-30), s, np.float32(0.0))
+    return np.where(mx <= F32_MAX, s, np.float32(np.nan)).astype(np.float32)
+
+
+def row_scales_f32(X: np.ndarray, axis: int) -> np.ndarray:
+    a = np.abs(X.astype(np.float32))
+    a = np.where(np.isnan(a), np.float32(np.inf), a)
+    return scale_for_max(a.max(axis=axis))
+
+
+def digit_words(X: np.ndarray, s: np.ndarray) -> np.ndarray:
+    """Z = rint(x 2^16 / s) + bias as the device computes it: one fp32 FMA with
+    1.5 * 2^23 (the product is exact, so FMA == multiply then add) and the
+    float's bit pattern minus (magic bits - bias)."""
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.where(s > 0, np.float32(65536.0) / s, s).astype(np.float32)
+    prod = (X.astype(np.float32) * inv).astype(np.float32)
+    f = (prod + MAGIC).astype(np.float32)
+    return f.view(np.int32).astype(np.int64) - (MAGIC_BITS - BIAS)
+
+
+def digits_from_words(Z: np.ndarray):
+    """q1 = byte 2 (two's complement), q2 = byte 1 - 128, q3 = byte 0 - 128."""
+    zu = Z.astype(np.int64) & 0xFFFFFFFF
+    q1 = ((zu >> 16) & 0xFF).astype(np.uint8).view(np.int8).astype(np.int64)
+    q2 = ((zu >> 8) & 0xFF).astype(np.int64) - 128
+    q3 = (zu & 0xFF).astype(np.int64) - 128
+    return q1, q2, q3
+
+
+def byte_perm(x: np.ndarray, y: np.ndarray, sel: int) -> np.ndarray:
+    """__byte_perm(x, y, sel) for selectors without the sign-replicate bit:
+    result byte n = byte (sel >> 4n) & 7 of the 8-byte value {y:x}."""
+    src = (y.astype(np.uint64) << np.uint64(32)) | (x.astype(np.uint64) & np.uint64(0xFFFFFFFF))
+    out = np.zeros(x.shape, dtype=np.uint64)
+    for n in range(4):
+        b = (sel >> (4 * n)) & 7
+        out |= ((src >> np.uint64(8 * b)) & np.uint64(0xFF)) << np.uint64(8 * n)
+    return out.astype(np.uint32)
+
+
+def pack_digits(z0, z1, z2, z3):
+    """ozd::pack_digits: four digit words -> the three packed int8 slices."""
+    u = [np.asarray(z, dtype=np.int64).astype(np.uint32) for z in (z0, z1, z2, z3)]
+    h1, l1 = byte_perm(u[0], u[1], 0x0062), byte_perm(u[2], u[3], 0x0062)
+    h2, l2 = byte_perm(u[0], u[1], 0x0051), byte_perm(u[2], u[3], 0x0051)
+    h3, l3 = byte_perm(u[0], u[1], 0x0040), byte_perm(u[2], u[3], 0x0040)
+    w1 = byte_perm(h1, l1, 0x5410)
+    w2 = byte_perm(h2, l2, 0x5410) ^ np.uint32(0x80808080)
+    w3 = byte_perm(h3, l3, 0x5410) ^ np.uint32(0x80808080)
+    return w1, w2, w3
+
+
+def split_f32(X: np.ndarray, axis: int):
+    """Scales along ``axis`` (the contraction index) and the three digit planes."""
+    s = row_scales_f32(X, axis)
+    Z = digit_words(X, np.expand_dims(s, axis))
+    return s, digits_from_words(Z)
+
+
+def levels3(QA, QB):
+    """L2, L3, L4 of two digit sets (rows . rows^T), exact in int64."""
+    a1, a2, a3 = QA
+    b1, b2, b3 = QB
+    return a1 @ b1.T, a1 @ b2.T + a2 @ b1.T, a1 @ b3.T + a2 @ b2.T + a3 @ b1.T
+
+
+def level_combine(l2, l3, l4):
+    """ozd::level_combine in fp32 (after the exact int32 sums)."""
+    f = np.float32
+    return (l2.astype(f) + l3.astype(f) * f(1.0 / 256.0)) + l4.astype(f) * f(1.0 / 65536.0)
+
+
+# ---------------------------------------------------------------- fp64 digits
+# (csrc/mp2_i8x5.cuh split_kernel: 5 digits of 2^32; csrc/ozaki_gemm64.cuh: 6 of 2^40)
+
+def split_f64(X: np.ndarray, axis: int, ndig: int):
+    a = np.abs(X)
+    a = np.where(np.isnan(a), np.inf, a)
+    m = a.max(axis=axis)
+    _, ex = np.frexp(m)
+    s = np.where(m > 1.0e-290, np.ldexp(1.0, ex - 6), 0.0)
+    s = np.where(m <= np.finfo(np.float64).max, s, np.nan)
+    shift = 8 * (ndig - 1)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.where(s > 0, np.ldexp(1.0, shift) / s, 0.0)
+    Y = np.rint(X * np.expand_dims(inv, axis)).astype(np.int64)  # half-even, as __double2ll_rn
+    bias = sum(0x80 << (8 * d) for d in range(ndig - 1))
+    z = Y + bias
+    q = [((z >> shift) & 0xFF).astype(np.uint8).view(np.int8).astype(np.int64)]
+    for d in range(1, ndig):
+        q.append(((z >> (shift - 8 * d)) & 0xFF).astype(np.int64) - 128)
+    return s, Y, q
+
+
+def levels_upto(QA, QB, max_sum):
+    """Level l = sum of q_a q'_b over a + b = l + 2 (1-based digits), a + b <= max_sum."""
+    n = len(QA)
+    lev = []
+    for l in range(max_sum - 1):
+        acc = 0
+        for a in range(1, n + 1):
+            b = l + 2 - a
+            if 1 <= b <= n:
+                acc = acc + QA[a - 1] @ QB[b - 1].T
+        lev.append(acc)
+    return lev
+
+
+def combine64(lev):
+    return sum(L.astype(np.float64) * 2.0 ** (-8 * l) for l, L in enumerate(lev))
+
+
+# ---------------------------------------------------------------- energies
+
+def energy_from_T(T, eo, ev):
+    """sum over ordered pairs of T_ab (2 T_ab - T_ba) / D in fp64 (T[i][j] = T_ij)."""
+    nocc = eo.shape[0]
+    e = 0.0
+    for i in range(nocc):
+        for j in range(nocc):
+            t = T[i][j].astype(np.float64)
+            d = (eo[i] + eo[j]) - ev[:, None] - ev[None, :]
+            e += float((t * (2 * t - t.T) / d).sum())
+    return e
+
+
+def mp2_emulated_f32(B, eo, ev):
+    B = B.astype(np.float32)
+    s, Q = split_f32(B, axis=2)
+    nocc = B.shape[0]
+    T = [[None] * nocc for _ in range(nocc)]
+    for i in range(nocc):
+        for j in range(nocc):
+            lv = levels3([q[i] for q in Q], [q[j] for q in Q])
+            for L in lv:  # every level sum must fit in int32
+                assert np.abs(L).max(initial=0) < 2**31
+            T[i][j] = level_combine(*lv) * (s[i][:, None] * s[j][None, :]).astype(np.float32)
+    return energy_from_T(T, eo.astype(np.float64), ev.astype(np.float64))
+
+
+def mp2_emulated_f64(B, eo, ev):
+    B = B.astype(np.float64)
+    s, _, Q = split_f64(B, axis=2, ndig=5)
+    nocc = B.shape[0]
+    T = [[None] * nocc for _ in range(nocc)]
+    for i in range(nocc):
+        for j in range(nocc):
+            lev = levels_upto([q[i] for q in Q], [q[j] for q in Q], 7)
+            assert len(lev) == 6 and sum(
+                1 for a in range(1, 6) for b in range(1, 6) if a + b <= 7) == 19
+            T[i][j] = combine64(lev) * (s[i][:, None] * s[j][None, :])
+    return energy_from_T(T, eo.astype(np.float64), ev.astype(np.float64))
+
+
+# ---------------------------------------------------------------- tests
+
+def test_int32_level_bounds_match_the_abi_limits():
+    """Largest |level| per k-term times K stays below 2^31 exactly up to the
+    limits the C ABI enforces, and one more term could overflow."""
+    d1, dn = 64, 128  # |q1| <= 64, |q2..| <= 128
+    per_k_f32 = max(d1 * d1, 2 * d1 * dn, 2 * d1 * dn + dn * dn)
+    assert per_k_f32 == 32768
+    assert 65535 * per_k_f32 < 2**31 <= 65536 * per_k_f32
+
+    def per_k(ndig, max_sum):
+        worst = 0
+        for s_ in range(2, max_sum + 1):
+            worst = max(worst, sum((d1 if a == 1 else dn) * (d1 if s_ - a == 1 else dn)
+                                   for a in range(1, ndig + 1) if 1 <= s_ - a <= ndig))
+        return worst
+
+    assert per_k(5, 7) * 32767 < 2**31 <= per_k(5, 7) * 32768      # mp2d: K <= 32767
+    assert per_k(6, 7) * 26214 < 2**31 <= per_k(6, 7) * 26215      # oz64: K <= 26214
+    from trntensor_b200.dispatch import OZAKI_F64_MAX_K, OZAKI_GEMM_F64_MAX_K, OZAKI_MAX_K
+    assert (OZAKI_MAX_K, OZAKI_F64_MAX_K, OZAKI_GEMM_F64_MAX_K) == (65535, 32767, 26214)
+
+
+def test_fp32_digits_reconstruct_and_stay_in_range():
+    rng = np.random.default_rng(0)
+    X = np.concatenate([
+        rng.standard_normal((64, 257)),
+        rng.standard_normal((8, 257)) * 1e-20,
+        rng.standard_normal((8, 257)) * 3e30,
+        np.ldexp(1.0, rng.integers(-40, 40, (8, 257))) * rng.choice([-1, 1], (8, 257)),
+    ]).astype(np.float32)
+    X[3, 5] = np.float32(np.ldexp(1.0, 7))  # an exact power of two as the row max
+    s, (q1, q2, q3) = split_f32(X, axis=1)
+    assert np.all(q1 >= -64) and np.all(q1 <= 64)
+    assert np.all(q2 >= -128) and np.all(q2 <= 127) and np.all(q3 >= -128) and np.all(q3 <= 127)
+    Y = q1 * 65536 + q2 * 256 + q3
+    exact = X.astype(np.float64) * (65536.0 / s.astype(np.float64))[:, None]
+    assert np.abs(Y - exact).max() <= 0.5  # one rounding: |r| <= s / 2^17
+    rec = s[:, None].astype(np.float64) * Y / 65536.0
+    assert np.all(np.abs(rec - X) <= s[:, None] / 2**17)
+    # |x / s| < 64 for every row, and the scale is the smallest such power of two
+    assert np.all(np.abs(X).max(axis=1) < 64 * s) and np.all(np.abs(X).max(axis=1) >= 32 * s)
+
+
+def test_fp32_zero_and_nonfinite_rows():
+    X = np.zeros((3, 8), dtype=np.float32)
+    X[1, 2] = np.inf
+    X[2, 4] = np.nan
+    s = row_scales_f32(X, axis=1)
+    assert s[0] == 0.0 and np.isnan(s[1]) and np.isnan(s[2])
+    assert scale_for_max(np.float32(1e-31)) == 0.0
+
+
+def test_pack_digits_byte_layout():
+    """Slice word w_d holds digit d of values 0..3 in bytes 0..3, as int8."""
+    rng = np.random.default_rng(1)
+    X = (rng.standard_normal((4, 1000)) * 10).astype(np.float32)
+    s = row_scales_f32(X.T, axis=1)  # one scale per column of 4 values
+    Z = digit_words(X, s[None, :])
+    w = pack_digits(Z[0], Z[1], Z[2], Z[3])
+    q = digits_from_words(Z)
+    for d in range(3):
+        got = w[d].view(np.uint8).reshape(-1, 4).view(np.int8).astype(np.int64)
+        np.testing.assert_array_equal(got, q[d].T)
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_fp32_mp2_energy_meets_tolerance(golden, name):
+    B, eo, ev = (t.numpy() for t in mp2_case_inputs(golden, name))
+    if B.shape[0] > 16:
+        pytest.skip("pair loop too long for the CPU emulation")
+    e = mp2_emulated_f32(B, eo, ev)
+    ref = float(golden[f"{name}/e_fp64"])
+    assert abs(e - ref) <= 1e-6 * abs(ref)
+
+
+@pytest.mark.parametrize("name", MP2_CASES)
+def test_fp64_five_digit_mp2_energy_meets_tolerance(golden, name):
+    B, eo, ev = (t.numpy() for t in mp2_case_inputs(golden, name))
+    if B.shape[0] > 16:
+        pytest.skip("pair loop too long for the CPU emulation")
+    e = mp2_emulated_f64(B, eo, ev)
+    ref = float(golden[f"{name}/e_fp64"])
+    assert abs(e - ref) <= 1e-12 * abs(ref)
+
+
+def test_fp64_digits_are_exact():
+    rng = np.random.default_rng(2)
+    X = rng.standard_normal((32, 300)) * np.ldexp(1.0, rng.integers(-30, 30, (32, 1)))
+    for ndig, shift in ((5, 32), (6, 40)):
+        s, Y, q = split_f64(X, axis=1, ndig=ndig)
+        assert np.abs(Y).max() < 2 ** (shift + 6)
+        assert q[0].min() >= -64 and q[0].max() <= 64
+        assert all(d.min() >= -128 and d.max() <= 127 for d in q[1:])
+        rebuilt = sum(d << (shift - 8 * k) for k, d in enumerate(q))
+        np.testing.assert_array_equal(rebuilt, Y)
+
+
+def _gemm_cols_f32(A, Bm):
+    """C = A^T B for (K, M), (K, N) operands with column scales (csrc/ozaki_gemm.cuh)."""
+    sa, QA = split_f32(A, axis=0)
+    sb, QB = split_f32(Bm, axis=0)
+    lv = levels3([q.T for q in QA], [q.T for q in QB])
+    return level_combine(*lv) * (sa[:, None] * sb[None, :]).astype(np.float32)
+
+
+def _gemm_cols_f64(A, Bm):
+    sa, _, QA = split_f64(A, axis=0, ndig=6)
+    sb, _, QB = split_f64(Bm, axis=0, ndig=6)
+    lev = levels_upto([q.T for q in QA], [q.T for q in QB], 7)
+    return combine64(lev) * (sa[:, None] * sb[None, :])
+
+
+def _ao2mo_emulated(eri, C_occ, C_vir, gemm, dt):
+    nbf, _, naux = eri.shape
+    nocc = C_occ.shape[1]
+    eri = eri.astype(dt)
+    inter = gemm(C_occ.astype(dt), eri.reshape(nbf, nbf * naux)).astype(dt)  # (nocc, nbf*naux)
+    inter = inter.reshape(nocc, nbf, naux)
+    return np.stack([gemm(C_vir.astype(dt), inter[i]) for i in range(nocc)])
+
+
+@pytest.mark.parametrize("name", [n for n in AO_CASES if n != "config1"])
+def test_ao2mo_column_split_meets_tolerance(golden, name):
+    eri, C_occ, C_vir = (t.numpy() for t in ao_case_inputs(golden, name)[:3])
+    ref = golden[f"{name}/B_fp64"]
+    b32 = _ao2mo_emulated(eri, C_occ, C_vir, _gemm_cols_f32, np.float32)
+    assert np.abs(b32 - ref).max() <= 1e-5 * np.abs(ref).max()
+    b64 = _ao2mo_emulated(eri, C_occ, C_vir, _gemm_cols_f64, np.float64)
+    assert np.abs(b64 - ref).max() <= 1e-12 * np.abs(ref).max()

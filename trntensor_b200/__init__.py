@@ -3,7 +3,8 @@
 Drop-in for the trnsci/trntensor 0.4.0 public namespace
 (trntensor/__init__.py:30-51): ``import trntensor_b200 as trntensor``.
 ``mp2_energy`` and ``ao_to_mo_transform`` run hand-written sm_100a kernels
-(tcgen05 3xTF32 / fp64) through the C ABI in ``include/trntensor_b200.h``;
+(int8 Ozaki-split ``tcgen05.mma`` with exact int32 accumulation, for fp32
+and for fp64) through the C ABI in ``include/trntensor_b200.h``;
 ``einsum``/``multi_einsum``/planning stay host Python. The tensor
 decompositions are outside this build and raise ``NotImplementedError``.
 """

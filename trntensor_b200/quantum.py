@@ -3,7 +3,8 @@
 Same signatures, validation and error messages as the reference
 (trntensor/quantum.py:21-84 and 103-185), plus an optional ``precision=``
 keyword with ``trntensor.einsum``'s meaning (trntensor/einsum.py:108-116):
-``"fast"`` computes in the input dtype (fp32 via 3xTF32 tensor cores),
+``"fast"`` computes in the input dtype (fp32-level accuracy from int8
+tensor-core GEMMs on three Ozaki digits per value, accumulated exactly),
 ``"kahan"`` computes in fp64 and returns the input dtype, ``"dd"`` raises
 ``NotImplementedError``.
 
