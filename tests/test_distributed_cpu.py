@@ -99,3 +99,34 @@ def test_failed_rank_does_not_hang_the_others():
     res = dict((r, g) for r, g, _ in _run(2, "fail"))
     assert res[1] == "raised"
     assert res[0] == "error"
+
+
+def test_host_row_chunks_cover_each_ranks_pairs():
+    """Host-resident B: a rank copies row chunks last-first and runs, after
+    each chunk, the pairs whose rows are all resident. The chunks' pair ranges
+    must partition the rank's pair range, every pair must have both rows
+    copied by then, and the rows copied must be exactly those that
+    host_bytes_needed counts."""
+    from trntensor_b200.dispatch import chunk_pair_range, first_row_of_pair, host_row_chunks
+
+    for nocc in (1, 2, 5, 17, 64, 256):
+        npairs = nocc * (nocc + 1) // 2
+        ids = [(i, j) for i in range(nocc) for j in range(i, nocc)]
+        for world in (1, 2, 3, 8):
+            for rank in range(world):
+                pb, pe = distributed.pair_range(npairs, rank, world)
+                chunks = host_row_chunks(nocc, pb, pe)
+                covered = []
+                resident_from = nocc
+                for a, b in chunks:
+                    assert b == resident_from and a < b  # contiguous, last rows first
+                    resident_from = a
+                    lo, hi = chunk_pair_range(nocc, pb, pe, a, b)
+                    for p in range(lo, hi):
+                        i, j = ids[p]
+                        assert first_row_of_pair(p, nocc) == i
+                        assert i >= resident_from and j >= resident_from
+                    covered.extend(range(lo, hi))
+                assert sorted(covered) == list(range(pb, pe))  # each pair exactly once
+                rows = nocc - resident_from if chunks else 0
+                assert rows * 7 * 3 * 4 == distributed.host_bytes_needed(nocc, 7, 3, rank, world)

@@ -230,6 +230,32 @@ def first_row_of_pair(p: int, nocc: int) -> int:
     return lo
 
 
+def host_row_chunks(nocc: int, pb: int, pe: int, chunks: int = 16) -> list[tuple[int, int]]:
+    """Row chunks [a, b) of B in copy order (last rows first) for pairs [pb, pe).
+
+    Only rows from the first row of pair ``pb`` on are needed; they are cut
+    into about ``chunks`` equal pieces."""
+    if pe <= pb:
+        return []
+    i0 = first_row_of_pair(pb, nocc)
+    step = max(1, -(-(nocc - i0) // chunks))
+    bounds = []
+    b = nocc
+    while b > i0:
+        a = max(i0, b - step)
+        bounds.append((a, b))
+        b = a
+    return bounds
+
+
+def chunk_pair_range(nocc: int, pb: int, pe: int, a: int, b: int) -> tuple[int, int]:
+    """Pair ids of [pb, pe) whose first row lies in [a, b): once rows a..nocc-1
+    are resident these pairs (i >= a, j >= i) have both their rows."""
+    lo = max(pb, pair_offset(a, nocc))
+    hi = min(pe, pair_offset(b, nocc) if b < nocc else nocc * (nocc + 1) // 2)
+    return lo, hi
+
+
 def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
     """fp32 DF-MP2 energy of host-resident pinned B with the copy overlapped.
 
@@ -255,14 +281,7 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
     q_ptr = ws.data_ptr()
     s_ptr = ws.data_ptr() + qbytes
     Bd = torch.empty((nocc, nvir, naux), dtype=torch.float32, device=dev)
-    i0 = first_row_of_pair(pb, nocc)
-    step = max(1, -(-(nocc - i0) // chunks))
-    bounds = []
-    b = nocc
-    while b > i0:
-        a = max(i0, b - step)
-        bounds.append((a, b))
-        b = a
+    bounds = host_row_chunks(nocc, pb, pe, chunks)
     energies = torch.zeros(len(bounds), dtype=torch.float64, device=dev)
     status = torch.zeros(len(bounds), dtype=torch.int32, device=dev)
     copy_stream = torch.cuda.Stream(dev)
@@ -276,8 +295,7 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
         _lib.check(lib.tt_split_i8_rows(ctypes.c_void_p(Bd.data_ptr()), ctypes.c_void_p(q_ptr),
                                         ctypes.c_void_p(s_ptr), a * nvir, (b - a) * nvir,
                                         rows_total, naux, pad, sp), "tt_split_i8_rows")
-        lo = max(pb, pair_offset(a, nocc))
-        hi = min(pe, pair_offset(b, nocc) if b < nocc else nocc * (nocc + 1) // 2)
+        lo, hi = chunk_pair_range(nocc, pb, pe, a, b)
         if hi > lo:
             st = lib.tt_mp2_energy_presplit_i8(
                 ctypes.c_void_p(q_ptr), ctypes.c_void_p(s_ptr), pad, _ptr(eo), _ptr(ev), nocc,
