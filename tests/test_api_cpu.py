@@ -189,6 +189,35 @@ class TestCAbi:
         assert not missing, missing
         assert declared == set(_lib.SIGNATURES), declared ^ set(_lib.SIGNATURES)
 
+    def test_ctypes_signatures_match_the_header(self):
+        """Every prototype's return and parameter types agree with the ctypes
+        binding: a missing or mistyped argument would pass garbage through the
+        ABI without any error."""
+        c_types = {"int": ctypes.c_int, "long long": ctypes.c_longlong,
+                   "size_t": ctypes.c_size_t, "void": None}
+        protos = {}
+        for h in sorted((ROOT / "include").glob("*.h")):
+            txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+            txt = re.sub(r"^\s*#.*$", "", txt, flags=re.M)
+            txt = txt.replace('extern "C" {', "")
+            for ret, name, args in re.findall(r"([\w\s\*]+?)\b(tt_\w+)\s*\(([^)]*)\)\s*;", txt):
+                protos[name] = (ret.split(";")[-1].split("}")[-1].strip(),
+                                [a.strip() for a in args.split(",")])
+        assert set(protos) == set(_lib.SIGNATURES)
+
+        def py_type(decl, is_ret):
+            decl = re.sub(r"\bconst\b", "", decl).strip()
+            if "*" in decl:
+                return ctypes.c_char_p if (is_ret and decl.startswith("char")) else ctypes.c_void_p
+            base = " ".join(w for w in decl.split() if w in ("int", "long", "size_t", "void"))
+            return c_types[base]
+
+        for name, (ret, args) in protos.items():
+            restype, argtypes = _lib.SIGNATURES[name]
+            assert py_type(ret, True) is restype, (name, ret)
+            want = [] if args in ([""], ["void"]) else [py_type(a, False) for a in args]
+            assert want == list(argtypes), (name, args)
+
     def test_host_only_calls(self):
         lib = _lib.load()
         assert lib.tt_version() >= 100
