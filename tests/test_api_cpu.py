@@ -189,6 +189,20 @@ class TestCAbi:
         assert not missing, missing
         assert declared == set(_lib.SIGNATURES), declared ^ set(_lib.SIGNATURES)
 
+    def test_library_exports_nothing_undeclared(self):
+        """Every tt_* symbol the shipped library exports is declared in
+        include/*.h: no hidden entry points (and no hidden global state behind
+        them)."""
+        import subprocess
+
+        out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.library_path())],
+                             capture_output=True, text=True, check=True).stdout
+        exported = {ln.split()[-1] for ln in out.splitlines()
+                    if len(ln.split()) == 3 and ln.split()[1] == "T"}
+        exported = {n for n in exported if n.startswith("tt_")}
+        assert exported, "nm found no tt_* exports"
+        assert exported == self._declared(), exported ^ self._declared()
+
     def test_ctypes_signatures_match_the_header(self):
         """Every prototype's return and parameter types agree with the ctypes
         binding: a missing or mistyped argument would pass garbage through the
@@ -244,3 +258,22 @@ def test_ao2mo_pattern_match():
     # on CPU the generic path still runs (and agrees with torch.einsum)
     torch.testing.assert_close(tt.einsum("mi,na,mnP->iaP", co, cv, e),
                                torch.einsum("mi,na,mnP->iaP", co, cv, e))
+
+
+def test_greedy_path_avoids_outer_products():
+    """At the AO->MO shapes the cheapest union is the (m,i) x (n,a) outer
+    product, which shares no index; the planner contracts a connected pair
+    first. Chains keep the reference's cheapest-first choice."""
+    from trntensor_b200.plan import _greedy_path_search
+
+    sizes = {"m": 1024, "n": 1024, "i": 128, "a": 896, "P": 3072}
+    path = _greedy_path_search(["mi", "na", "mnP"], "iaP", sizes)
+    assert path[0] in ((0, 2), (1, 2))
+    # the reference's pinned cases (tests/test_plan.py:154-166)
+    assert _greedy_path_search(["ij", "jk", "kl", "lm"], "im",
+                               {"i": 100, "j": 200, "k": 5, "l": 50, "m": 3})[0] == (2, 3)
+    # only disjoint pairs left: an outer product is still allowed
+    assert _greedy_path_search(["i", "j", "k"], "ijk", {"i": 2, "j": 3, "k": 4})[0] == (0, 1)
+    A, B, C = torch.randn(5, 3), torch.randn(4, 3), torch.randn(5, 4, 6)
+    torch.testing.assert_close(tt.einsum("mi,na,mnP->iaP", A, B, C),
+                               torch.einsum("mi,na,mnP->iaP", A, B, C))

@@ -76,6 +76,13 @@ def test_empty_inputs(cuda_ok):
     e = tt.mp2_energy(torch.zeros(0, 4, 5, device="cuda"), torch.zeros(0, device="cuda"),
                       torch.zeros(4, device="cuda"))
     assert e.item() == 0.0 and e.device.type == "cuda"
+    for shape in ((0, 4, 5), (3, 0, 5), (3, 4, 0)):
+        Bz = torch.zeros(*shape, device="cuda")
+        eo, ev = torch.zeros(shape[0], device="cuda"), torch.zeros(shape[1], device="cuda")
+        p = tt.mp2_pair_energies(Bz, eo, ev)
+        assert p.shape == (shape[0], shape[0]) and p.dtype == torch.float64 and not p.any()
+        from trntensor_b200 import distributed
+        assert distributed.mp2_energy(Bz, eo, ev).item() == 0.0
     B = tt.ao_to_mo_transform(torch.zeros(4, 4, 3, device="cuda"), torch.zeros(4, 0, device="cuda"),
                               torch.zeros(4, 2, device="cuda"))
     assert B.shape == (0, 2, 3)

@@ -243,9 +243,12 @@ int ao2mo_simt(const T* eri, const T* C_occ, const T* C_vir, int nbf, int nocc, 
 }  // namespace
 }  // namespace tt
 
-// Debug hook: per-CTA wait-cycle counters of TT_OZC_PROFILE builds.
+// Per-CTA wait-cycle counters exist only in TT_OZC_PROFILE builds (a
+// measurement build, never the shipped library).
+#ifdef TT_OZC_PROFILE
 static long long* g_ozc_prof = nullptr;
 extern "C" void tt_debug_set_ao2mo_profile_buffer(long long* buf) { g_ozc_prof = buf; }
+#endif
 
 extern "C" {
 
@@ -338,7 +341,11 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     pc.tiles_m = (nocc + ozc::kTile - 1) / ozc::kTile;
     pc.tiles_n = (int)((ncol + ozc::kTile - 1) / ozc::kTile);
     pc.err = dev_status;
+#ifdef TT_OZC_PROFILE
     pc.prof = g_ozc_prof;
+#else
+    pc.prof = nullptr;
+#endif
     const char* hint = std::getenv("TRNTENSOR_B200_AO2MO_L2HINT");
     pc.l2hint = !(hint != nullptr && hint[0] == '0');  // on unless set to 0
     const long long tiles = (long long)pc.tiles_m * pc.tiles_n;

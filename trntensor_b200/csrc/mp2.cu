@@ -149,9 +149,13 @@ static int launch_chunks(mp2::Params& p, long long pair_begin, long long pair_en
   return TT_OK;
 }
 
-// Debug hook: per-CTA wait-cycle counters of TT_MP2_PROFILE builds.
+// Per-CTA wait-cycle counters exist only in TT_MP2_PROFILE builds (a
+// measurement build, never the shipped library): there the buffer is set
+// once by tt_debug_set_profile_buffer before any launch.
+#ifdef TT_MP2_PROFILE
 static long long* g_mp2_prof = nullptr;
 extern "C" void tt_debug_set_profile_buffer(long long* buf) { g_mp2_prof = buf; }
+#endif
 
 extern "C" {
 
@@ -246,7 +250,11 @@ int tt_mp2_energy_presplit_i8(const signed char* Q, const float* scale, int naux
   p.energy = energy;
   p.pair_partials = pair_partials;
   p.err = dev_status;
+#ifdef TT_MP2_PROFILE
   p.prof = g_mp2_prof;
+#else
+  p.prof = nullptr;
+#endif
   // The pair range is issued as consecutive launches of about kWavesPerLaunch
   // waves each, accumulating into the same energy. A single persistent launch
   // lets CTAs drift apart over thousands of items (one- and two-phase items

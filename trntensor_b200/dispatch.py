@@ -30,11 +30,14 @@ _VALID_BACKENDS = ("auto", "cuda", "pytorch", "nki")
 def set_backend(backend: str) -> None:
     """Select the executor for the generic ``einsum`` strategies.
 
-    Mirrors trntensor/nki/dispatch.py:94-101. ``"auto"``/``"cuda"`` route the
-    matmul-shaped plans to CUDA tensors' native kernels, ``"pytorch"`` keeps
-    them on whatever device the operands live on. ``"nki"`` raises, exactly as
-    the reference does on a host without neuronxcc. The two DF-MP2 primitives
-    always run on the sm_100a library.
+    Mirrors trntensor/nki/dispatch.py:94-101. ``"auto"`` and ``"pytorch"``
+    run matmul/bmm plans with torch on the operands' device (cuBLAS fp32 for
+    CUDA tensors: elementwise fp32 rounding, like the reference's default).
+    ``"cuda"`` opts CUDA fp32 operands into the int8 tensor-core GEMM
+    (``tt_gemm_f32``): 2-3x cuBLAS fp32 throughput, with an error bounded
+    per row and column rather than per element (see ``_cuda_gemm``).
+    ``"nki"`` raises, exactly as the reference does on a host without
+    neuronxcc. The two DF-MP2 primitives always run on the sm_100a library.
     """
     global _backend
     if backend not in _VALID_BACKENDS:
@@ -380,9 +383,19 @@ def _operand_layout(X: torch.Tensor, kmajor_if_contiguous: bool):
 
 
 def _cuda_gemm(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
-    """fp32 (batched) A @ B on int8 tensor cores (fp32-level accuracy).
+    """fp32 (batched) A @ B on int8 tensor cores (``set_backend("cuda")``).
 
     A: (M, K) or (b, M, K); B: (K, N) or (b, K, N); CUDA fp32 tensors.
+
+    Accuracy contract: each row of A and each column of B carries one
+    power-of-two scale (from its largest magnitude, M_i and M_j) and three
+    int8 digits, so the error is bounded per row and column, not per element:
+    |C_ij - (AB)_ij| <= 2^-19 (M_i |B_:j|_1 + |A_i:|_1 M_j)
+    + 2^-20 sqrt(K) M_i M_j. For rows and columns of similar magnitudes that
+    is fp32 accuracy; an entry far below its row's (column's) largest keeps
+    fewer bits than fp32 would give it. A row or column with a largest
+    magnitude below 1e-30 counts as zero, and one holding inf or NaN makes its
+    whole output row or column NaN (fp32 would give inf in some places).
     """
     lib = _lib.load()
     dev = A.device

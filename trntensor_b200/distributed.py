@@ -72,6 +72,8 @@ def mp2_energy(
     _validate_mp2(B, eps_occ, eps_vir, precision)
     rank, world = _world(group)
     nocc = int(B.shape[0])
+    if B.numel() == 0:  # same shapes on every rank: all of them return here
+        return B.new_zeros(())
     npairs = nocc * (nocc + 1) // 2
     e, _ = _cuda_mp2_energy(
         B, eps_occ, eps_vir, precision=precision, pair_range=pair_range(npairs, rank, world)

@@ -139,7 +139,9 @@ def _tensor_core_ok(plan: ContractionPlan, *ops: torch.Tensor) -> bool:
 
 
 def _execute_path(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.Tensor:
-    """Walk ``plan.contraction_path``; each step is a binary torch.einsum."""
+    """Walk ``plan.contraction_path``; each step is a binary ``einsum`` call of
+    this module (as trntensor/einsum.py:151-158 does), so a matmul- or
+    bmm-shaped step gets its own plan and executor."""
     lhs, out = _parse_subscripts(subscripts)
     terms = lhs.split(",")
     ops = list(operands)
@@ -150,7 +152,8 @@ def _execute_path(subscripts: str, operands: tuple, plan: ContractionPlan) -> to
         else:
             later = set(out).union(*(set(t) for k, t in enumerate(terms) if k not in (x, y)))
             res_term = "".join(dict.fromkeys(c for c in terms[x] + terms[y] if c in later))
-        res = torch.einsum(f"{terms[x]},{terms[y]}->{res_term}", ops[x], ops[y])
+        res = einsum(f"{terms[x]},{terms[y]}->{res_term}", ops[x], ops[y],
+                     precision=plan.precision)
         ops = [o for k, o in enumerate(ops) if k not in (x, y)] + [res]
         terms = [t for k, t in enumerate(terms) if k not in (x, y)] + [res_term]
     return ops[0]

@@ -8,7 +8,9 @@ for 3+ operands (plan.py:188-243, same cost: product of the sizes of the
 pair's index union) and ``estimate_flops`` (plan.py:317-332, multiply-adds).
 
 ``ContractionPlan.backend`` names the executor: ``"cuda"`` when a
-matmul/bmm plan's operands live on a CUDA device, else ``"pytorch"``.
+matmul/bmm plan's operands live on a CUDA device and ``set_backend("cuda")``
+selected the int8 tensor-core GEMM, else ``"pytorch"`` (torch on the
+operands' device: cuBLAS fp32 for CUDA tensors, as the reference's default).
 """
 
 from __future__ import annotations
@@ -108,7 +110,7 @@ def _backend_for(strategy: str, operands: tuple) -> str:
     ):
         from .dispatch import get_backend
 
-        return "cuda" if get_backend() in ("auto", "cuda") else "pytorch"
+        return "cuda" if get_backend() == "cuda" else "pytorch"
     return "pytorch"
 
 
@@ -151,7 +153,12 @@ def _greedy_path_search(
     """Greedy pairwise order (opt_einsum convention: indices into the current list).
 
     Each step contracts the pair whose index union has the smallest product
-    of sizes; the intermediate keeps the indices still needed later, sorted.
+    of sizes (the reference's cost, trntensor/plan.py:222-232); the
+    intermediate keeps the indices still needed later, sorted. Unlike the
+    reference, a pair that shares no index (an outer product) is taken only
+    when no pair shares one: at the AO->MO shapes the reference's rule picks
+    the (m,i) x (n,a) outer product first, a (nbf, nocc, nbf, nvir)
+    intermediate of 481 GB at nbf 1024. The value is the same either way.
     """
     ops = list(input_list)
     path: list[tuple[int, int]] = []
@@ -164,8 +171,9 @@ def _greedy_path_search(
                 cost = 1
                 for ch in union:
                     cost *= size_map.get(ch, 1)
-                if best is None or cost < best[0]:
-                    best = (cost, x, y, union & keep)
+                key = (not (set(ops[x]) & set(ops[y])), cost)
+                if best is None or key < best[0]:
+                    best = (key, x, y, union & keep)
         _, x, y, inter = best
         path.append((x, y))
         ops = [o for k, o in enumerate(ops) if k not in (x, y)] + ["".join(sorted(inter))]

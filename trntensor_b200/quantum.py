@@ -81,6 +81,9 @@ def mp2_pair_energies(
     trntensor/nki/dispatch.py:283); ``.sum()`` of it is ``mp2_energy``.
     """
     _validate_mp2(B, eps_occ, eps_vir, precision)
+    nocc, nvir, naux = (int(x) for x in B.shape)
+    if nocc == 0 or nvir == 0 or naux == 0:
+        return torch.zeros((nocc, nocc), dtype=torch.float64, device=B.device)
     _, partials = _cuda_mp2_energy(B, eps_occ, eps_vir, precision=precision, return_partials=True)
     return partials.to(B.device)
 
