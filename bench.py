@@ -12,8 +12,16 @@ per step / step time (max over ranks).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-``--impl reference`` times the reference's CPU algorithm (the numpy port in
-oracle/, the reference being pure Python/torch) on host cores, rank 0 only.
+``--impl reference`` times the reference's own CPU implementation of the
+path, ``trntensor.quantum._cpu_mp2_energy`` (installed unmodified under
+baseline/_ref), on the host cores, rank 0 only, on sampled pairs of the same
+workload; the numpy restatement in oracle/ stands in only if that install is
+missing.
+
+Inputs: config 4's B is drawn on the host row by row
+(``trntensor_b200.inputs.mp2_inputs_rowwise``, seed 0) outside the timed
+region, so that 64 pair energies can be checked against fp64 oracle values
+computed from the same rows (tests/golden/config4_pairs.json).
 """
 
 from __future__ import annotations
@@ -45,8 +53,8 @@ CONFIGS = {
 METRIC = "DF-MP2 pair-contraction TFLOP/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of the mp2::energy_kernel
 # launches of one step, per unordered pair: ncu with --cache-control none on
-# the same tiles with nocc = 32 (528 pairs, 16 launches): 74.0 GB per step
-# (profiles/mp2_energy_kernel_config4.md). Traffic grows with the pairs.
+# the same tiles with nocc = 32 (528 pairs, 16 launches): 74.0 GB per step.
+# Traffic grows with the pairs.
 TRAFFIC_BYTES_PER_PAIR = 140.1e6
 
 
@@ -196,51 +204,82 @@ def _blas_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_pair_sample(c, seconds, B_rows=None, seed=0):
-    """Time the oracle port of the reference's loop body on sampled ordered pairs.
+def cpu_info() -> dict:
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"model": model, "host_cpus": os.cpu_count(), "torch_threads": torch.get_num_threads()}
 
-    Returns (seconds per ordered pair, pairs timed). ``B_rows(i)`` gives
-    B[i] as a numpy (nvir, naux) fp32 array.
-    """
+
+def reference_cpu_mp2():
+    """The reference's own CPU energy, ``trntensor.quantum._cpu_mp2_energy``
+    (trntensor/quantum.py:87-100), from the unmodified install under
+    baseline/_ref; None when that install is absent."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "trntensor" / "quantum.py").exists():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    try:
+        from trntensor.quantum import _cpu_mp2_energy
+    except Exception:
+        return None
+    return _cpu_mp2_energy
+
+
+_ROW_CACHE: dict[tuple, torch.Tensor] = {}
+
+
+def cpu_pair_sample(c, seconds, seed=0, rows_fn=None):
+    """Seconds per ordered (i, j) pair of the reference's CPU path on sampled
+    pairs of config ``c``: the median over calls of ``_cpu_mp2_energy`` on the
+    two-row slice B[[i, j]] (one call computes the 4 ordered pairs of {i, j}^2,
+    all of equal cost, so a call's time / 4 is one pair's). Rows come from the
+    row-wise recipe (``rows_fn(i)`` overrides). Falls back to the numpy
+    restatement in oracle/ (kind "port") without the reference install."""
     import numpy as np
 
-    from oracle import oracle
+    from trntensor_b200.inputs import mp2_eps_rowwise, mp2_row
 
     nocc, nvir, naux = c["nocc"], c["nvir"], c["naux"]
+    eo, ev = mp2_eps_rowwise(nocc, nvir, 0)
     rng = np.random.default_rng(seed)
-    g = torch.Generator().manual_seed(seed)
-    eo = (torch.rand(nocc, generator=g, dtype=torch.float64) * 1.5 - 2.0).float().numpy()
-    ev = (torch.rand(nvir, generator=g, dtype=torch.float64) * 2.8 + 0.2).float().numpy()
-    cache: dict[int, np.ndarray] = {}
+    occ = [int(x) for x in rng.choice(nocc, size=min(nocc, 6), replace=False)]
+    def row(i):
+        key = (nocc, nvir, naux, i, rows_fn is None)
+        if key not in _ROW_CACHE:
+            _ROW_CACHE[key] = torch.from_numpy(rows_fn(i) if rows_fn else mp2_row(i, nvir, naux, 0))
+        return _ROW_CACHE[key]
 
-    def rows(i):
-        if i not in cache:
-            if B_rows is not None:
-                cache[i] = B_rows(i)
-            else:
-                gi = torch.Generator().manual_seed(seed * 100003 + i)
-                cache[i] = (torch.randn(nvir, naux, generator=gi) / math.sqrt(naux)).numpy()
-        return cache[i]
-
-    occ = rng.choice(nocc, size=min(nocc, 8), replace=False)
-    pairs = [(int(a), int(b)) for a in occ for b in occ]
+    pairs = [(a, b) for k, a in enumerate(occ) for b in occ[k + 1:]]
     rng.shuffle(pairs)
-    Bsub = np.zeros((nocc, 1, 1), dtype=np.float32)  # placeholder for shape only
-    del Bsub
-    # warm-up one pair (BLAS thread pool start-up)
-    i0, j0 = pairs[0]
-    Bij = np.stack([rows(i0), rows(j0)])
-    oracle.mp2_pair_energy(Bij, eo[[i0, j0]], ev, 0, 1)
+    fn = reference_cpu_mp2()
+    kind = "reference" if fn is not None else "port"
+    if fn is None:
+        from oracle import oracle
+
+        def fn(Bij, eo2, ev_):  # noqa: E731  (same loop body, numpy BLAS)
+            return oracle.mp2_energy_loop(Bij.numpy(), eo2.numpy(), ev_.numpy())[0]
+
+    def call(i, j):
+        Bij = torch.stack([row(i), row(j)])
+        t0 = time.perf_counter()
+        fn(Bij, eo[[i, j]], ev)
+        return (time.perf_counter() - t0) / 4.0
+
+    call(*pairs[0])  # warm-up (BLAS thread pool)
     times = []
     t_end = time.perf_counter() + seconds
     for i, j in pairs:
-        Bij = np.stack([rows(i), rows(j)])
-        t0 = time.perf_counter()
-        oracle.mp2_pair_energy(Bij, eo[[i, j]], ev, 0, 1)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end and len(times) >= 4:
+        times.append(call(i, j))
+        if time.perf_counter() > t_end and len(times) >= 3:
             break
-    return statistics.mean(times), len(times)
+    return statistics.median(times), len(times), kind
 
 
 def cpu_metric(c, t_pair):
@@ -257,17 +296,21 @@ def run_reference(args, rank, world):
         cpu_pair_sample(c, 0.0, seed=1)
     vals, secs = [], []
     per_step_seconds = max(1.0, args.cpu_seconds / max(1, args.steps))
-    npairs_total = 0
+    ncalls = 0
+    kind = "port"
     for k in range(args.steps):
         t0 = time.perf_counter()
-        t_pair, n = cpu_pair_sample(c, per_step_seconds, seed=2 + k)
+        t_pair, n, kind = cpu_pair_sample(c, per_step_seconds, seed=2 + k)
         secs.append(time.perf_counter() - t0)
-        npairs_total += n
+        ncalls += n
         vals.append(cpu_metric(c, t_pair)[0])
-    value = statistics.mean(vals)
-    cores = _blas_threads()
-    sample = (f"{npairs_total} ordered (i,j) pairs of config {args.config} over {args.steps} steps "
-              f"(reference loop body, fp32, numpy BLAS); extrapolated to all nocc^2 ordered pairs")
+    value = statistics.median(vals)
+    info = cpu_info()
+    what = ("trntensor.quantum._cpu_mp2_energy (reference, unmodified, torch CPU fp32)"
+            if kind == "reference" else "numpy restatement of the reference loop body")
+    sample = (f"{ncalls} calls of {what} on two-row slices B[[i,j]] of config {args.config} "
+              f"(4 ordered pairs each) over {args.steps} steps; per step the median per-pair "
+              f"time, extrapolated to all nocc^2 ordered pairs; value = median over steps")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -276,15 +319,15 @@ def run_reference(args, rank, world):
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": 1e3 * statistics.mean(secs),
+        "ms_per_step": 1e3 * statistics.median(secs),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded, BASELINE config distributions)",
+        "data": "synthetic (row-wise seeded, BASELINE config distributions)",
         "config": {"workload": f"mp2_config{args.config}", **c, "sampled": True},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": info["torch_threads"],
+                         "kind": kind, "sample": sample, **info},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -336,6 +379,45 @@ def measured_peaks():
 
 
 AO_CONFIG = dict(nbf=1024, nocc=128, nvir=896, naux=3072)
+# DRAM bytes (read + write) of one transform per aux index at config 3's
+# nbf / nocc / nvir, summed over its kernels: ncu dram__bytes_read.sum +
+# dram__bytes_write.sum of one call at naux 512 (the traffic grows with naux:
+# every kernel works per aux column), divided by 512.
+AO_TRAFFIC_BYTES_PER_AUX = None
+
+
+def int8_peak_from_driver(peaks: dict) -> tuple[float, str]:
+    """Dense int8 TOPS for a kernel timed inside a long step: twice the
+    driver's sustained bf16 GEMM rate (B200's dense int8 rate is twice its
+    bf16 rate), else twice the pool's fallback sustained bf16 figure."""
+    bf = peaks.get("bf16_tflops_sustained")
+    if bf:
+        return 2.0 * bf, "2 x bf16_tflops_sustained (MEASURED_PEAKS.json)"
+    return 2.0 * 1400.0, "2 x 1.4 PFLOP/s bf16 sustained (fallback)"
+
+
+def ao2mo_roofline(alg_bytes: float, flops: float, ms: float, naux_local: int) -> dict:
+    """Roofline of one rank's transform: the slower of HBM (algorithmic bytes
+    at the measured copy bandwidth) and the tensor cores (6 int8 GEMMs per
+    fp32-equivalent GEMM at the int8 peak); frac = that floor / measured time."""
+    peaks = measured_peaks()
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    int8, src = int8_peak_from_driver(peaks)
+    t_hbm = alg_bytes / (hbm * 1e9)
+    t_tc = 6.0 * flops / (int8 * 1e12)
+    t = ms / 1e3
+    traffic = AO_TRAFFIC_BYTES_PER_AUX * naux_local if AO_TRAFFIC_BYTES_PER_AUX else None
+    if t_tc >= t_hbm:
+        out = {"bound": "tensor", "achieved": flops / t / 1e12, "peak": int8 / 6.0,
+               "unit": "TFLOP/s", "frac": t_tc / t}
+    else:
+        out = {"bound": "hbm", "achieved": alg_bytes / t / 1e9, "peak": hbm, "unit": "GB/s",
+               "frac": t_hbm / t}
+    out.update({"traffic": traffic, "floor_ms_hbm": t_hbm * 1e3, "floor_ms_tensor": t_tc * 1e3,
+                "hbm_frac": t_hbm / t, "tensor_frac": t_tc / t,
+                "peak_source": f"hbm_gbs (MEASURED_PEAKS.json); int8 = {src}; "
+                               "frac of measured"})
+    return out
 
 
 def measure_ao2mo(args, rank, world, local):
@@ -386,6 +468,7 @@ def measure_ao2mo(args, rank, world, local):
            "TFLOP_per_s": flops / ms / 1e9, "algorithmic_bytes": alg_bytes, "flops": flops,
            "parallelism": f"aux index split over {world} GPU(s), no communication",
            "kernels": "int8 Ozaki tcgen05 GEMMs (column-scaled slices), two steps"}
+    res["roofline"] = ao2mo_roofline(alg_bytes / world, flops / world, ms, nl)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
 
@@ -437,11 +520,98 @@ def measure_ao2mo(args, rank, world, local):
     return res
 
 
+def host_inputs(c, rank, world, local):
+    """Row-wise seeded fp32 B (nocc, nvir, naux) in page-locked host memory.
+
+    With several ranks on the node the buffer is one shared-memory file
+    mapped by every rank (each draws 1/world of the rows, then registers the
+    mapping with CUDA), so the host holds one copy of B instead of one per
+    rank; without room in /dev/shm, a private pinned buffer per rank.
+    Returns (B, eps_occ, eps_vir, info)."""
+    import shutil
+
+    from trntensor_b200.inputs import mp2_eps_rowwise, mp2_inputs_rowwise
+
+    nocc, nvir, naux = c["nocc"], c["nvir"], c["naux"]
+    numel = nocc * nvir * naux
+    nbytes = numel * 4
+    shm = Path("/dev/shm")
+    use_shm = world > 1 and shm.is_dir() and shutil.disk_usage(shm).free > 1.2 * nbytes
+    if use_shm:
+        tag = os.environ.get("TORCHELASTIC_RUN_ID") or os.environ.get("MASTER_PORT", "0")
+        path = shm / f"trntensor_b200_bench_B_{tag}_{nocc}_{nvir}_{naux}"
+        if local == 0:
+            with open(path, "wb") as f:
+                f.truncate(nbytes)
+        barrier(world)
+        B = torch.from_file(str(path), shared=True, size=numel, dtype=torch.float32)
+        B = B.view(nocc, nvir, naux)
+        mp2_inputs_rowwise(nocc, nvir, naux, seed=0, out=B,
+                           rows=range(local, nocc, max(1, world)))
+        barrier(world)
+        err = torch.cuda.cudart().cudaHostRegister(B.data_ptr(), nbytes, 0)
+        if local == 0:
+            path.unlink(missing_ok=True)  # the mappings stay valid until every rank exits
+        info = {"host_buffer": "shared /dev/shm mapping, cudaHostRegister",
+                "register_status": int(err) if not isinstance(err, int) else err}
+    else:
+        B = torch.empty((nocc, nvir, naux), dtype=torch.float32, pin_memory=True)
+        mp2_inputs_rowwise(nocc, nvir, naux, seed=0, out=B)
+        info = {"host_buffer": "pinned (cudaHostAlloc) per rank"}
+    eo, ev = mp2_eps_rowwise(nocc, nvir, 0)
+    info["pinned"] = bool(B.is_pinned())
+    return B, eo, ev, info
+
+
+def oracle_check(lib, q, sc, naux_pad, eo, ev, c, pb, pe, dev, world):
+    """The fixture's fp64 oracle pair energies (tests/golden/config4_pairs.json,
+    same row-wise inputs) against the kernel's per-pair partials for the
+    pairs in this rank's range; max over ranks of the worst relative error."""
+    from trntensor_b200.dispatch import pair_offset
+
+    fx_path = ROOT / "tests" / "golden" / "config4_pairs.json"
+    nocc, nvir = c["nocc"], c["nvir"]
+    if not fx_path.exists():
+        return None
+    fx = json.loads(fx_path.read_text())
+    if (fx["config"]["nocc"], fx["config"]["nvir"], fx["config"]["naux"]) != (
+            nocc, nvir, c["naux"]):
+        return None
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    part = torch.zeros((nocc, nocc), dtype=torch.float64, device=dev)
+    energy = torch.empty((), dtype=torch.float64, device=dev)
+    status = torch.empty((), dtype=torch.int32, device=dev)
+    mine = []
+    for i, j, e in fx["pairs"]:
+        p = pair_offset(i, nocc) + (j - i)
+        if not pb <= p < pe:
+            continue
+        one = torch.empty((nocc, nocc), dtype=torch.float64, device=dev)
+        from trntensor_b200 import _lib
+
+        _lib.check(lib.tt_mp2_energy_presplit_i8(P(q), P(sc), naux_pad, P(eo), P(ev), nocc, nvir,
+                                                 p, p + 1, P(energy), P(one), P(status), sp),
+                   "check")
+        part[i, j] = one[i, j]
+        mine.append((i, j, e))
+    torch.cuda.synchronize(dev)
+    worst = 0.0
+    for i, j, e in mine:
+        worst = max(worst, abs(part[i, j].item() - e) / abs(e))
+    n = torch.tensor([float(len(mine))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(n)
+    worst = max_over_ranks(worst, world, dev)
+    return {"pairs": int(n.item()), "max_rel_err_vs_fp64_oracle": worst, "tolerance": 1e-6,
+            "source": "tests/golden/config4_pairs.json (oracle.mp2_pair_energy in fp64 on the "
+                      "same rows)", "pass": worst <= 1e-6}
+
+
 def run_ours(args, rank, world, local):
     import trntensor_b200 as tt
     from trntensor_b200 import _lib, distributed
-    from trntensor_b200.dispatch import _cuda_mp2_energy, first_row_of_pair, pair_offset
-    from trntensor_b200.inputs import mp2_inputs
+    from trntensor_b200.dispatch import _cuda_mp2_energy, pair_offset
 
     lib = _lib.load()
     dev = torch.device("cuda", local)
@@ -452,7 +622,11 @@ def run_ours(args, rank, world, local):
     my_flops = (pe - pb) * flops_per_pair(c)
     job_flops = npairs * flops_per_pair(c)
 
-    B, eo, ev = mp2_inputs(nocc, nvir, naux, seed=0, dtype=torch.float32, device=dev)
+    t_gen = time.perf_counter()
+    Bh, eoh, evh, host_info = host_inputs(c, rank, world, local)
+    host_info["generate_s"] = time.perf_counter() - t_gen
+    B = Bh.to(dev)
+    eo, ev = eoh.to(dev), evh.to(dev)
     naux_pad = (naux + 63) // 64 * 64
     rows = nocc * nvir
     q = torch.empty(3, rows, naux_pad, dtype=torch.int8, device=dev)
@@ -517,11 +691,8 @@ def run_ours(args, rank, world, local):
         diag = sum(1 for i in range(nocc) if lo <= pair_offset(i, nocc) < hi)
         energy_launches += 1 + (1 if (hi - lo - diag) * (nblk * (nblk - 1) // 2) > 0 else 0)
 
-    # sanity check: 8 pairs against the fp64 CUDA-core kernel
-    e_chk, _ = _cuda_mp2_energy(B, eo, ev, pair_range=(pb, min(pe, pb + 8)))
-    e_ref, _ = _cuda_mp2_energy(B.double(), eo.double(), ev.double(),
-                                pair_range=(pb, min(pe, pb + 8)), kernel="simt")
-    check_rel = abs(e_chk.item() - e_ref.item()) / abs(e_ref.item())
+    # parity: the fixture's 64 oracle pairs (config 4), per pair
+    check = oracle_check(lib, q, sc, naux_pad, eo, ev, c, pb, pe, dev, world)
 
     # fp64 path (precision="kahan"): rate on a slice of the same workload, for
     # the five-digit int8 tensor-core kernel (split included) and the CUDA-core
@@ -555,22 +726,13 @@ def run_ours(args, rank, world, local):
         del Bd, eod, evd
         torch.cuda.empty_cache()
 
-    # roofline of the dominant kernel
-    int8 = measure_int8_peak(dev)
+    # roofline of the dominant kernel: peak from the driver's measured peaks
     peaks = measured_peaks()
-    bf16 = peaks.get("bf16_tflops")
-    if int8 is not None:
-        int8_burst, int8_peak = int8
-        # the energy kernel runs for seconds under the 1 kW cap: the
-        # denominator is the sustained rate of a plain int8 GEMM
-        peak_src = ("int8 dense GEMM measured in this run (torch._int_mm, cuBLASLt, 8192^3, "
-                    "back to back for 3 s: sustained under the power cap) / 6")
-    else:
-        int8_burst = int8_peak = 2.0 * (peaks.get("bf16_tflops_sustained") or bf16 or 1375.5)
-        peak_src = "2 x bf16 dense sustained (MEASURED_PEAKS.json) / 6"
+    int8_peak, peak_src = int8_peak_from_driver(peaks)
     peak_eff = int8_peak / 6.0
     achieved = my_flops / kernel_s / 1e12
-    # per launch: the step's energy launches average (the ratio is the same)
+    int8_lt = measure_int8_peak(dev)  # cuBLASLt int8 GEMM, side figure
+    bf16 = peaks.get("bf16_tflops")
     my_pairs = pe - pb
     roof = {
         "bound": "tensor",
@@ -585,14 +747,16 @@ def run_ours(args, rank, world, local):
         "launches_per_step": energy_launches,
         "kernel_ms": kernel_s * 1e3 / max(1, energy_launches),
         "kernel_ms_per_step": kernel_s * 1e3,
-        "peak_source": peak_src,
+        "peak_source": f"{peak_src} / 6 int8 GEMMs per fp32-equivalent GEMM; frac of measured",
         "int8_tops_peak": int8_peak,
-        "int8_tops_burst": int8_burst,
-        "frac_of_burst": achieved / (int8_burst / 6.0),
         "int8_tops_achieved": 6.0 * achieved,
         "flops_per_launch": my_flops / max(1, energy_launches),
-        "flops_convention": "unique pairs i<=j x 2 nvir^2 naux (fp32-equivalent); the kernel runs 6 int8 slice GEMMs per fp32 GEMM",
+        "flops_convention": "unique pairs i<=j x 2 nvir^2 naux (fp32-equivalent); the kernel "
+                            "runs 6 int8 slice GEMMs per fp32 GEMM",
     }
+    if int8_lt is not None:
+        roof["cublaslt_int8_tops_burst"], roof["cublaslt_int8_tops_sustained"] = int8_lt
+        roof["frac_of_cublaslt_sustained"] = achieved / (int8_lt[1] / 6.0)
     if bf16:
         roof["north_star_3xtf32_peak"] = bf16 / 2.0 / 3.0
         roof["north_star_frac"] = achieved / (bf16 / 2.0 / 3.0)
@@ -600,16 +764,8 @@ def run_ours(args, rank, world, local):
     # end-to-end: public API, host (pinned) inputs, result back on the host
     e2e = None
     if not args.no_e2e:
-        # Host copy of B in pinned memory, written straight from the device
-        # (no pageable staging copy: at N ranks that would hold N x 11.3 GB of
-        # host memory twice). The call reads only rows first_row(pb).. of it,
-        # so a rank fills those; the rest of the buffer stays unwritten.
-        i0 = first_row_of_pair(pb, nocc) if pe > pb else nocc
-        Bh = torch.empty(B.shape, dtype=B.dtype, pin_memory=True)
-        Bh[i0:].copy_(B[i0:])
-        q = None  # slices no longer needed; the API allocates its own workspace
+        del q
         torch.cuda.empty_cache()
-        eoh, evh = eo.cpu(), ev.cpu()
         api = tt.mp2_energy if world == 1 else distributed.mp2_energy
         api(Bh, eoh, evh)  # warm-up (allocator, workspace)
         torch.cuda.synchronize(dev)
@@ -629,22 +785,24 @@ def run_ours(args, rank, world, local):
                "d2h_bytes_per_step": 8 * world, "ms_per_step": t_e2e * 1e3,
                "api": "trntensor_b200.mp2_energy" if world == 1 else
                       "trntensor_b200.distributed.mp2_energy",
-               "energy": float(e_host.item())}
+               "energy": float(e_host.item()), **host_info}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        Bc = B.cpu()
-        t_pair, n = cpu_pair_sample(c, args.cpu_seconds, B_rows=lambda i: Bc[i].numpy())
+        t_pair, n, kind = cpu_pair_sample(c, args.cpu_seconds,
+                                          rows_fn=lambda i: Bh[i].numpy())
         v, t_job = cpu_metric(c, t_pair)
-        cpu = {"value": v, "unit": "TFLOP/s", "cores": _blas_threads(), "kind": "port",
-               "sample": f"{n} ordered (i,j) pairs of config {args.config} timed with the numpy "
-                         f"port of the reference loop body (fp32); extrapolated to all "
-                         f"{nocc}^2 ordered pairs = {t_job:.0f} s",
-               "host_cpus": os.cpu_count()}
+        what = ("trntensor.quantum._cpu_mp2_energy (reference as shipped, torch CPU fp32)"
+                if kind == "reference" else "numpy restatement of the reference loop body")
+        info = cpu_info()
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": info["torch_threads"], "kind": kind,
+               "sample": f"{n} calls of {what} on two-row slices of config {args.config} "
+                         f"(4 ordered pairs each; median per-pair time), extrapolated to all "
+                         f"{nocc}^2 ordered pairs = {t_job:.0f} s", **info}
 
     ao = None
     if not args.no_ao2mo:
-        del B, q, sc
+        del B, sc
         torch.cuda.empty_cache()
         try:
             ao = measure_ao2mo(args, rank, world, local)
@@ -665,7 +823,7 @@ def run_ours(args, rank, world, local):
             "vs_baseline": None,
             "dtype": "f32",
             "arith": "int8 Ozaki slices (3), int32 tensor-core accumulation, fp32/fp64 epilogue",
-            "data": "synthetic (seeded on device, BASELINE config distributions)",
+            "data": "synthetic (row-wise seeded on the host, BASELINE config distributions)",
             "config": {"workload": f"mp2_config{args.config}", "nocc": nocc, "nvir": nvir,
                        "naux": naux, "unique_pairs": npairs, "flops_per_step": job_flops,
                        "l2": (f"B {nocc * nvir * naux * 4 / 1e9:.3g} GB fp32, slices "
@@ -675,7 +833,7 @@ def run_ours(args, rank, world, local):
                        "parallelism": f"pairs sharded over {world} GPU(s), B replicated, "
                                       f"fp64 all-reduce"},
             "energy": energy_value,
-            "check": {"pairs": 8, "rel_err_vs_fp64_kernel": check_rel},
+            "check": check,
             "fp64": fp64,
             "roofline": roof,
             "cpu_baseline": cpu,

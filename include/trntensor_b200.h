@@ -78,6 +78,22 @@ int tt_mp2_energy_f32(const float* B, const float* eps_occ, const float* eps_vir
 int tt_split_i8(const float* x, signed char* q, float* scale, long long rows, int cols,
                 int cols_pad, void* stream);
 
+/* Accuracy statistics of the three-digit format of tt_split_i8 over rows x
+ * cols (row-major fp32), ADDED into stats[0..2] (device fp64; the caller
+ * zeroes them, so that a matrix can be summed piecewise):
+ *   stats[0] += sum_r n_r s_r^2 u2_r,  stats[1] += sum_r n_r s_r^2 u3_r,
+ *   stats[2] += sum_r n_r,
+ * n_r = sum of squares of row r, s_r its scale, u2_r / u3_r the sums of
+ * squares of its second / third digits. With K = cols,
+ *   est = 2 sqrt(2^-47 stats[0] stats[1] / K) / (stats[2]^2 / K)
+ * estimates the relative energy error tt_mp2_energy_f32 makes by dropping
+ * the q2 q3 digit products (an over-estimate by 10-100x on the cases
+ * measured). Rows whose entries span many decades, or hold a few entries far
+ * above the rest, raise it; Gaussian rows give ~2e-7 or less. The Python
+ * layer computes the energy with the five-digit kernel when est > 1e-6.
+ * No counterpart in the reference (its fp32 GEMM rounds per element). */
+int tt_mp2_range_stats_f32(const float* x, long long rows, int cols, double* stats, void* stream);
+
 /* tt_split_i8 for rows [row_begin, row_begin + row_count) of a total_rows x
  * cols matrix, written into the slice planes of the whole matrix (plane
  * stride total_rows * cols_pad). Lets a caller split B as its rows arrive

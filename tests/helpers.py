@@ -62,3 +62,31 @@ def ao_case_inputs(golden, name):
 
 
 __all__ = ["mp2_inputs", "ao2mo_inputs"]
+
+
+def wide_mp2_inputs(shape, seed, decades=6.0, spike=0.0, frac=0.0):
+    """MP2 inputs whose B rows span ``decades`` decades along the aux index
+    (B[i,a,:] *= logspace(-decades, 0, naux)[perm], a fresh permutation per
+    row); a fraction ``frac`` of rows also gets one spike: ``spike`` times the
+    row's largest magnitude, or (spike == 0) the row becomes one-hot 0.3."""
+    nocc, nvir, naux = shape
+    B, eo, ev = mp2_inputs(nocc, nvir, naux, seed=seed)
+    B = B.double().numpy()
+    rng = np.random.default_rng(seed + 100)
+    ls = np.logspace(-decades, 0, naux)
+    for i in range(nocc):
+        for a in range(nvir):
+            B[i, a] *= ls[rng.permutation(naux)]
+    rows = rng.random((nocc, nvir)) < frac
+    for i, a in zip(*np.nonzero(rows)):
+        P = rng.integers(naux)
+        if spike == 0:
+            B[i, a] = 0.0
+            B[i, a, P] = 0.3
+        else:
+            B[i, a, P] = spike * np.abs(B[i, a]).max()
+    return torch.from_numpy(B.astype(np.float32)), eo, ev
+
+
+WIDE_CASES = [(6, 0, 0.0), (6, 0, 0.05), (6, 10, 0.1), (6, 1e3, 0.1), (3, 100, 0.1),
+              (0, 10, 0.1)]

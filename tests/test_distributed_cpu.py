@@ -101,13 +101,14 @@ def test_failed_rank_does_not_hang_the_others():
     assert res[0] == "error"
 
 
-def test_host_row_chunks_cover_each_ranks_pairs():
-    """Host-resident B: a rank copies row chunks last-first and runs, after
-    each chunk, the pairs whose rows are all resident. The chunks' pair ranges
-    must partition the rank's pair range, every pair must have both rows
-    copied by then, and the rows copied must be exactly those that
-    host_bytes_needed counts."""
-    from trntensor_b200.dispatch import chunk_pair_range, first_row_of_pair, host_row_chunks
+def test_host_copy_plan_covers_each_ranks_pairs():
+    """Host-resident B: a rank copies row chunks in host_copy_plan's order and
+    runs, after each chunk, the pair ranges listed with it. Those ranges must
+    partition the rank's pair range, every pair must have both rows resident
+    by then, the rows copied must be exactly those host_bytes_needed counts,
+    and pairs must be runnable after at most two chunks (so that the copy
+    overlaps compute on every rank)."""
+    from trntensor_b200.dispatch import host_copy_plan
 
     for nocc in (1, 2, 5, 17, 64, 256):
         npairs = nocc * (nocc + 1) // 2
@@ -115,18 +116,27 @@ def test_host_row_chunks_cover_each_ranks_pairs():
         for world in (1, 2, 3, 8):
             for rank in range(world):
                 pb, pe = distributed.pair_range(npairs, rank, world)
-                chunks = host_row_chunks(nocc, pb, pe)
+                plan = host_copy_plan(nocc, pb, pe)
+                if pe <= pb:
+                    assert plan == []
+                    continue
+                resident: set[int] = set()
                 covered = []
-                resident_from = nocc
-                for a, b in chunks:
-                    assert b == resident_from and a < b  # contiguous, last rows first
-                    resident_from = a
-                    lo, hi = chunk_pair_range(nocc, pb, pe, a, b)
-                    for p in range(lo, hi):
-                        i, j = ids[p]
-                        assert first_row_of_pair(p, nocc) == i
-                        assert i >= resident_from and j >= resident_from
-                    covered.extend(range(lo, hi))
+                for step, (a, b, ranges) in enumerate(plan):
+                    assert a < b and not resident & set(range(a, b))  # each row once
+                    resident |= set(range(a, b))
+                    if step == 1 and nocc >= 17:
+                        assert covered or ranges, "nothing runnable after two chunks"
+                    for lo, hi in ranges:
+                        assert pb <= lo < hi <= pe
+                        for p in range(lo, hi):
+                            i, j = ids[p]
+                            assert i in resident and j in resident
+                        covered.extend(range(lo, hi))
                 assert sorted(covered) == list(range(pb, pe))  # each pair exactly once
-                rows = nocc - resident_from if chunks else 0
+                rows = len(resident)
+                assert resident == set(range(nocc - rows, nocc))
                 assert rows * 7 * 3 * 4 == distributed.host_bytes_needed(nocc, 7, 3, rank, world)
+                # launches stay few: one range per step when the rank owns the last row
+                nranges = sum(len(r) for _, _, r in plan)
+                assert nranges <= len(plan) * max(1, nocc // world + 2)

@@ -77,3 +77,23 @@ def test_config1_inputs_are_orthonormal_and_symmetric():
     C = torch.cat([co, cv], 1).double()
     torch.testing.assert_close(C.T @ C, torch.eye(128, dtype=torch.float64), atol=1e-6, rtol=0)
     torch.testing.assert_close(eri, eri.transpose(0, 1))
+
+
+def test_config4_fixture_reproduces():
+    """Two of the 64 config-4 pair energies recomputed from regenerated rows
+    (the row-wise recipe is deterministic), plus the stored row checksums."""
+    import json
+    from pathlib import Path
+
+    from trntensor_b200.inputs import mp2_eps_rowwise, mp2_row
+
+    fx = json.loads((Path(__file__).parent / "golden" / "config4_pairs.json").read_text())
+    c = fx["config"]
+    eo, ev = (t.numpy().astype(np.float64) for t in mp2_eps_rowwise(c["nocc"], c["nvir"], c["seed"]))
+    assert len(fx["pairs"]) >= 64
+    for i, j, e in (fx["pairs"][0], fx["pairs"][-1]):
+        Bij = np.stack([mp2_row(i, c["nvir"], c["naux"], c["seed"]),
+                        mp2_row(j, c["nvir"], c["naux"], c["seed"])]).astype(np.float64)
+        got = float(oracle.mp2_pair_energy(Bij, eo[[i, j]], ev, 0, 1))
+        assert got == pytest.approx(e, rel=1e-12)
+        assert Bij[0].sum() == pytest.approx(fx["row_sums"][str(i)], rel=1e-12)

@@ -326,3 +326,51 @@ def test_ao2mo_column_split_meets_tolerance(golden, name):
     assert np.abs(b32 - ref).max() <= 1e-5 * np.abs(ref).max()
     b64 = _ao2mo_emulated(eri, C_occ, C_vir, _gemm_cols_f64, np.float64)
     assert np.abs(b64 - ref).max() <= 1e-12 * np.abs(ref).max()
+
+
+# ---------------------------------------------------------------- wide rows
+
+def range_estimate(B):
+    """tt_mp2_range_stats_f32 + the host estimate, emulated (same digits)."""
+    x = B.reshape(-1, B.shape[-1]).astype(np.float32)
+    K = x.shape[1]
+    s, (_, q2, q3) = split_f32(x, axis=1)
+    s = s.astype(np.float64)
+    n = (x.astype(np.float64) ** 2).sum(1)
+    a2 = (n * s**2 * (q2.astype(np.float64) ** 2).sum(1)).sum()
+    a3 = (n * s**2 * (q3.astype(np.float64) ** 2).sum(1)).sum()
+    from trntensor_b200.dispatch import _wide_rows_estimate
+
+    return _wide_rows_estimate([a2, a3, n.sum()], K)
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_wide_rows_estimate_guards_the_three_digit_energy(seed):
+    """Rows spanning six decades along the aux index, one-hot rows and rows
+    with a spike far above the rest: wherever the range estimate keeps the
+    three-digit kernel (est <= 1e-6), its emulated energy is within 1e-6 of
+    fp64; Gaussian rows stay on the three-digit kernel. Cases above the
+    threshold run on the five-digit kernel (fp64 accuracy)."""
+    from tests.helpers import WIDE_CASES, wide_mp2_inputs
+    from trntensor_b200.dispatch import WIDE_ROWS_MAX_EST
+    from oracle import oracle
+
+    B, eo, ev = (t.numpy() for t in mp2_case_inputs_gauss(seed))
+    assert range_estimate(B) <= WIDE_ROWS_MAX_EST
+    kept = 0
+    for shape in ((3, 96, 384), (4, 150, 512)):
+        for dec, spike, frac in WIDE_CASES:
+            B, eo, ev = (t.numpy() for t in wide_mp2_inputs(shape, seed, dec, spike, frac))
+            est = range_estimate(B)
+            if est <= WIDE_ROWS_MAX_EST:
+                kept += 1
+                ref, _ = oracle.mp2_energy_fp64(B, eo, ev)
+                e = mp2_emulated_f32(B, eo, ev)
+                assert abs(e - ref) <= 1e-6 * abs(ref), (shape, dec, spike, frac, est)
+    assert kept >= 1  # six decades without spikes stays on three digits at 4 x 150 rows
+
+
+def mp2_case_inputs_gauss(seed):
+    from trntensor_b200.inputs import mp2_inputs
+
+    return mp2_inputs(3, 96, 384, seed=seed)

@@ -40,6 +40,7 @@ SIGNATURES: dict[str, tuple] = {
     "tt_mp2_tf32_workspace_bytes": (_SZ, [_I, _I, _I]),
     "tt_split_tf32": (_I, [_P, _P, _P, _LL, _I, _I, _P]),
     "tt_split_i8": (_I, [_P, _P, _P, _LL, _I, _I, _P]),
+    "tt_mp2_range_stats_f32": (_I, [_P, _LL, _I, _P, _P]),
     "tt_split_i8_rows": (_I, [_P, _P, _P, _LL, _LL, _LL, _I, _I, _P]),
     "tt_mp2_energy_f32": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _SZ, _P, _P, _P, _P]),
     "tt_mp2_energy_presplit_i8": (_I, [_P, _P, _I, _P, _P, _I, _I, _LL, _LL, _P, _P, _P, _P]),

@@ -19,15 +19,19 @@ int setup(int dev) {
   return once_per_device(g_flags, g_ok, dev, [dev]() -> int {
     if (cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return TT_ERR_CUDA;
-    if (cudaFuncSetAttribute(ozc::gemm_cvt_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             ozc::kSmemBytes) != cudaSuccess ||
-        cudaFuncSetAttribute(ozc::gemm_cvt_kernel<true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             ozc::kSmemBytes) != cudaSuccess ||
-        cudaFuncSetAttribute(ozc::gemm_cvt_split_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             ozc::kSmemBytes) != cudaSuccess)
+    const int sm32 = ozc::smem_bytes(3, 2), sm23 = ozc::smem_bytes(2, 3);
+    if (cudaFuncSetAttribute(ozc::gemm_cvt_kernel<false, 3, 2>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, sm32) != cudaSuccess ||
+        cudaFuncSetAttribute(ozc::gemm_cvt_kernel<true, 3, 2>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, sm32) != cudaSuccess ||
+        cudaFuncSetAttribute(ozc::gemm_cvt_split_kernel<3, 2>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, sm32) != cudaSuccess ||
+        cudaFuncSetAttribute(ozc::gemm_cvt_kernel<false, 2, 3>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, sm23) != cudaSuccess ||
+        cudaFuncSetAttribute(ozc::gemm_cvt_kernel<true, 2, 3>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, sm23) != cudaSuccess ||
+        cudaFuncSetAttribute(ozc::gemm_cvt_split_kernel<2, 3>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, sm23) != cudaSuccess)
       return TT_ERR_CUDA;
     {
       // A persistent grid of more clusters than fit at once would leave a
@@ -40,13 +44,18 @@ int setup(int dev) {
       attr[0].val.clusterDim.z = 1;
       cfg.gridDim = dim3(2 * 1024, 1, 1);
       cfg.blockDim = dim3(ozc::kThreads, 1, 1);
-      cfg.dynamicSmemBytes = ozc::kSmemBytes;
+      cfg.dynamicSmemBytes = sm32;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, ozc::gemm_cvt_split_kernel, &cfg) != cudaSuccess)
+      int n = 0, n23 = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, ozc::gemm_cvt_split_kernel<3, 2>, &cfg) !=
+          cudaSuccess)
         return TT_ERR_CUDA;
-      g_split_clusters[dev] = n;
+      cfg.dynamicSmemBytes = sm23;
+      if (cudaOccupancyMaxActiveClusters(&n23, ozc::gemm_cvt_split_kernel<2, 3>, &cfg) !=
+          cudaSuccess)
+        return TT_ERR_CUDA;
+      g_split_clusters[dev] = n < n23 ? n : n23;
     }
     if (cudaFuncSetAttribute(oz64::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              oz64::kSmemBytes) != cudaSuccess)
@@ -311,11 +320,18 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     // The GEMM splits fp32 eri tiles on chip. Its column scales come from the
     // GEMM itself (one HBM read of eri) when the contraction has more than two
     // 64-row chunks, else from a separate column-max pass.
+    // TRNTENSOR_B200_AO2MO_RING=23: 2 fp32 + 3 int8 ring slots instead of 3 + 2.
+    const char* rg = std::getenv("TRNTENSOR_B200_AO2MO_RING");
+    const bool ring23 = rg != nullptr && rg[0] == '2' && rg[1] == '3';
+    const int istages = ring23 ? 3 : 2;
+    // The fused column scales need more k-chunks than int8 slots per CTA
+    // (ozaki_gemm_cvt.cuh); with fewer, a separate column-max pass runs.
     const char* cm = std::getenv("TRNTENSOR_B200_AO2MO_COLMAX");
-    const bool fuse = nbf > 2 * ozc::kKC && !(cm != nullptr && cm[0] == '1');
-    // Split-K over CTA pairs (each half needs three k-chunks, as above).
+    const int nkc = (nbf + ozc::kKC - 1) / ozc::kKC;
+    const bool fuse = nkc >= istages + 1 && !(cm != nullptr && cm[0] == '1');
+    // Split-K over CTA pairs: each half needs as many k-chunks.
     const char* sk = std::getenv("TRNTENSOR_B200_AO2MO_SPLITK");
-    const bool split = fuse && nbf > 5 * ozc::kKC && g_split_clusters[dev] > 0 &&
+    const bool split = fuse && nkc / 2 >= istages + 1 && g_split_clusters[dev] > 0 &&
                        !(sk != nullptr && sk[0] == '0');
     if (!fuse) {
       const long long nblk = (pe + oz::kSplitCols - 1) / oz::kSplitCols;
@@ -350,13 +366,23 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     pc.l2hint = !(hint != nullptr && hint[0] == '0');  // on unless set to 0
     const long long tiles = (long long)pc.tiles_m * pc.tiles_n;
     const int grid = (int)(tiles < sms ? tiles : sms);
-    if (split) {
-      const long long cl = tiles < g_split_clusters[dev] ? tiles : g_split_clusters[dev];
-      ozc::gemm_cvt_split_kernel<<<(int)(2 * cl), ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
-    } else if (fuse)
-      ozc::gemm_cvt_kernel<true><<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
-    else
-      ozc::gemm_cvt_kernel<false><<<grid, ozc::kThreads, ozc::kSmemBytes, s>>>(ma, mx, pc);
+    const int smem = ozc::smem_bytes(ring23 ? 2 : 3, istages);
+    const long long cl = tiles < g_split_clusters[dev] ? tiles : g_split_clusters[dev];
+    if (ring23) {
+      if (split)
+        ozc::gemm_cvt_split_kernel<2, 3><<<(int)(2 * cl), ozc::kThreads, smem, s>>>(ma, mx, pc);
+      else if (fuse)
+        ozc::gemm_cvt_kernel<true, 2, 3><<<grid, ozc::kThreads, smem, s>>>(ma, mx, pc);
+      else
+        ozc::gemm_cvt_kernel<false, 2, 3><<<grid, ozc::kThreads, smem, s>>>(ma, mx, pc);
+    } else {
+      if (split)
+        ozc::gemm_cvt_split_kernel<3, 2><<<(int)(2 * cl), ozc::kThreads, smem, s>>>(ma, mx, pc);
+      else if (fuse)
+        ozc::gemm_cvt_kernel<true, 3, 2><<<grid, ozc::kThreads, smem, s>>>(ma, mx, pc);
+      else
+        ozc::gemm_cvt_kernel<false, 3, 2><<<grid, ozc::kThreads, smem, s>>>(ma, mx, pc);
+    }
     if ((st = cuda_status(cudaGetLastError()))) return st;
   }
   // slices of inter[i] (K = n, N = P), scales per (i, P)

@@ -197,6 +197,24 @@ int tt_split_i8_rows(const float* x, signed char* q, float* scale, long long row
   return cuda_status(cudaGetLastError());
 }
 
+int tt_mp2_range_stats_f32(const float* x, long long rows, int cols, double* stats,
+                           void* stream) {
+  if (!x || !stats) return TT_ERR_NULL;
+  if (rows < 0 || cols <= 0) return TT_ERR_SHAPE;
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st != TT_OK) return st;
+  st = mp2_setup(dev);
+  if (st != TT_OK) return st;
+  if (rows == 0) return TT_OK;
+  long long blocks = (rows + 7) / 8;
+  const long long cap = (long long)g_num_sms[dev] * 16;
+  if (blocks > cap) blocks = cap;
+  mp2::range_stats_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, rows, cols,
+                                                                             stats);
+  return cuda_status(cudaGetLastError());
+}
+
 int tt_split_i8(const float* x, signed char* q, float* scale, long long rows, int cols,
                 int cols_pad, void* stream) {
   return tt_split_i8_rows(x, q, scale, 0, rows, rows, cols, cols_pad, stream);

@@ -485,5 +485,62 @@ static __global__ void split_kernel(const float* __restrict__ x, int8_t* __restr
   }
 }
 
+// Statistics of the three-digit format over rows of x (one warp per row),
+// accumulated into acc[0..2] (fp64 atomics, one per block and value):
+//   acc[0] += sum_r n_r s_r^2 u2_r,  acc[1] += sum_r n_r s_r^2 u3_r,
+//   acc[2] += sum_r n_r,
+// n_r = sum_P x_rP^2, s_r the row scale and u2_r, u3_r the sums of squares of
+// the row's second and third digits. The digit products q2 q3' + q3 q2' are
+// the largest terms the energy kernel drops; these sums give the size of
+// that error relative to the energy when the rows' inner products behave
+// like random sums (the host turns them into an estimate). The digits are
+// computed exactly as split_kernel computes them.
+static __global__ void range_stats_kernel(const float* __restrict__ x, long long rows, int cols,
+                                          double* __restrict__ acc) {
+  __shared__ double part[3][8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  double a2 = 0.0, a3 = 0.0, an = 0.0;
+  for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + warp; r < rows; r += warps) {
+    const float* xr = x + r * cols;
+    float m = 0.f;
+    for (int c = lane; c < cols; c += 32) m = ozd::absmax(m, __ldg(xr + c));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float s = ozd::scale_for_max(m);
+    const float inv = ozd::inv_scale(s);
+    double n = 0.0, u2 = 0.0, u3 = 0.0;
+    for (int c = lane; c < cols; c += 32) {
+      const float v = __ldg(xr + c);
+      const int z = ozd::digit_word(v, inv);
+      const int q2 = ((z >> 8) & 0xFF) - 128, q3 = (z & 0xFF) - 128;
+      n += (double)v * v;
+      u2 += (double)(q2 * q2);
+      u3 += (double)(q3 * q3);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      n += __shfl_xor_sync(0xffffffffu, n, o);
+      u2 += __shfl_xor_sync(0xffffffffu, u2, o);
+      u3 += __shfl_xor_sync(0xffffffffu, u3, o);
+    }
+    const double w = n * (double)s * (double)s;
+    a2 += w * u2;
+    a3 += w * u3;
+    an += n;
+  }
+  if (lane == 0) {
+    part[0][warp] = a2;
+    part[1][warp] = a3;
+    part[2][warp] = an;
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[threadIdx.x][w];
+    atomicAdd(acc + threadIdx.x, t);
+  }
+}
+
 }  // namespace mp2
 }  // namespace tt

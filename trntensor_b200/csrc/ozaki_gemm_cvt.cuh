@@ -41,10 +41,16 @@ using oz::kTile;  // 128
 using oz::kKC;    // 64
 using oz::level_combine;
 
-// Ring depths: a 2-deep fp32 ring (with a 3-deep int8 ring) gave intermittently
-// wrong 32-byte column groups in the output and was not used; 3 + 2 is exact.
-constexpr int kFStages = 3;                   // fp32 landing ring (TMA -> converters)
-constexpr int kIStages = 2;                   // int8 ring (A by TMA, B by converters -> MMA)
+// Ring depths (template parameters of the kernel): kFStages fp32 landing
+// slots (TMA -> converters) and kIStages int8 slots (A by TMA, B by the
+// converters -> MMA). The default is 3 + 2; 2 + 3 (a deeper int8 ring in the
+// same shared memory) is built too and selected by TRNTENSOR_B200_AO2MO_RING=23.
+// The fused column scales need more k-chunks per CTA than int8 slots (the
+// scale double buffer is rewritten only after the MMA has started the next
+// tile, which a converter can only know from an int8 slot of that tile):
+// nkl >= kIStages + 1, which the host checks before choosing kFuse / kSplit.
+constexpr int kFStagesDefault = 3;
+constexpr int kIStagesDefault = 2;
 constexpr int kFBytes = kTile * kKC * 4;      // 32 KB fp32 tile
 constexpr int kARegion = 3 * kTile * kKC;     // 24 KB of A slices
 constexpr int kIBytes = 2 * kARegion;         // A and B slices: 48 KB
@@ -65,8 +71,12 @@ constexpr int kColPark = 3 * kTile;           // TMEM columns of the parked fp32
 constexpr int kARep = 8;                      // copies of the A slices (CTA b reads copy b % kARep)
 constexpr int kOutBytes = kTile * kQLd * 4;
 constexpr int kCMaxBytes = kCvtWarps * kTile * 4;  // per-warp column maxima (fused scales)
-constexpr int kSmemBytes = kFStages * kFBytes + kIStages * kIBytes + kOutBytes + 2 * kTile * 4 +
-                           kCMaxBytes + 2 * kTile * 4 + 1024 + 256;
+constexpr int smem_bytes(int fstages, int istages) {
+  return fstages * kFBytes + istages * kIBytes + kOutBytes + 2 * kTile * 4 + kCMaxBytes +
+         2 * kTile * 4 + 1024 + 256;
+}
+constexpr int kSmemBytes = smem_bytes(kFStagesDefault, kIStagesDefault);
+static_assert(smem_bytes(2, 3) <= 232448, "2 + 3 ring exceeds shared memory");
 constexpr int kCvtBar = 2;  // named barrier of the converter warps
 
 struct Params {
@@ -127,7 +137,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 // stores its partial tile, then rank 1 adds its own with red.global.add
 // (out_ready / out_done order the two and keep the barriers' phases apart).
 // C = (rank 0 partial) + (rank 1 partial): one fp32 rounding, deterministic.
-template <bool kFuse, bool kSplit>
+template <bool kFuse, bool kSplit, int kFStages, int kIStages>
 __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUtensorMap& mapX,
                                               const Params& p) {
   extern __shared__ uint8_t smem_raw[];
@@ -523,7 +533,7 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
       group_sync<32 * kCvtWarps, kCvtBar>();  // cmax free for the next tile
       return true;
     };
-    // kFuse requires K > 2 * kKC: then a converter that finishes tile r + 1
+    // kFuse requires nkl > kIStages: then a converter that finishes tile r + 1
     // (and writes the scales of tile r + 2 into escale[r & 1]) has waited for
     // an int8 slot that the MMA freed inside tile r + 1, so the epilogue has
     // already read escale[r & 1] and waited on scale_full[r & 1] for tile r.
@@ -610,17 +620,18 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
   }
 }
 
-template <bool kFuse>
+template <bool kFuse, int kFStages = kFStagesDefault, int kIStages = kIStagesDefault>
 static __global__ void __launch_bounds__(kThreads, 1)
     gemm_cvt_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX,
                     Params p) {
-  gemm_cvt_body<kFuse, false>(mapA, mapX, p);
+  gemm_cvt_body<kFuse, false, kFStages, kIStages>(mapA, mapX, p);
 }
 
+template <int kFStages = kFStagesDefault, int kIStages = kIStagesDefault>
 static __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_cvt_split_kernel(const __grid_constant__ CUtensorMap mapA,
                           const __grid_constant__ CUtensorMap mapX, Params p) {
-  gemm_cvt_body<true, true>(mapA, mapX, p);
+  gemm_cvt_body<true, true, kFStages, kIStages>(mapA, mapX, p);
 }
 
 }  // namespace ozc

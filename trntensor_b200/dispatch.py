@@ -15,6 +15,7 @@ device wrappers (trntensor/nki/dispatch.py:240-336, ``_nki_mp2_energy`` and
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 
 import torch
@@ -195,6 +196,14 @@ def _cuda_mp2_energy(
         _lib.check(st, "tt_mp2_energy_tf32x3")
         _check_status(dev_status, "tt_mp2_energy_tf32x3")
         return energy, partials
+    # Rows whose entries span many decades (or hold a few entries far above
+    # the rest) lose accuracy in the three-digit format; their energy is
+    # computed with the five-digit kernel (fp64 accuracy) instead.
+    stats = torch.zeros(3, dtype=torch.float64, device=dev)
+    _range_stats(lib, Bd, nocc * nvir, naux, stats, stream)
+    if _needs_more_digits(stats, naux):
+        return _cuda_mp2_energy(Bd, eo, ev, precision="kahan", pair_range=(pb, pe),
+                                return_partials=return_partials)
     ws_bytes = int(lib.tt_mp2_workspace_bytes(nocc, nvir, naux))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     dev_status = torch.empty((), dtype=torch.int32, device=dev)
@@ -233,41 +242,117 @@ def first_row_of_pair(p: int, nocc: int) -> int:
     return lo
 
 
-def host_row_chunks(nocc: int, pb: int, pe: int, chunks: int = 16) -> list[tuple[int, int]]:
-    """Row chunks [a, b) of B in copy order (last rows first) for pairs [pb, pe).
+def _merge(ranges: list[tuple[int, int]]) -> list[tuple[int, int]]:
+    out: list[tuple[int, int]] = []
+    for lo, hi in ranges:
+        if hi <= lo:
+            continue
+        if out and out[-1][1] == lo:
+            out[-1] = (out[-1][0], hi)
+        else:
+            out.append((lo, hi))
+    return out
 
-    Only rows from the first row of pair ``pb`` on are needed; they are cut
-    into about ``chunks`` equal pieces."""
+
+def host_copy_plan(nocc: int, pb: int, pe: int, chunks: int = 16):
+    """Copy order of a host B's rows for the pairs [pb, pe), and what to run.
+
+    Returns ``[(a, b, ranges), ...]``: copy rows [a, b), then run the pair id
+    ranges ``ranges`` (each half-open, row-major ids of i <= j), whose two
+    rows are resident by then and which no earlier step ran.
+
+    The range's pairs have i in [i0, i1] (its own rows) and j in [i, nocc).
+    Own rows are copied first, last ones first: once rows [a, i1] are in, the
+    pairs (i >= a, j <= i1) can run. Then the rows beyond i1 (needed only as
+    j) are copied first ones first, and each chunk [a, b) runs the pairs
+    (i in [i0, i1], j in [a, b)). The first pairs can thus start after one
+    chunk, whatever rows the range owns. With i1 = nocc - 1 (one GPU, the last
+    rank) every step is one contiguous id range; otherwise one range per own
+    row i, which is still few (about nocc / world own rows).
+    """
     if pe <= pb:
         return []
     i0 = first_row_of_pair(pb, nocc)
-    step = max(1, -(-(nocc - i0) // chunks))
-    bounds = []
-    b = nocc
+    i1 = first_row_of_pair(pe - 1, nocc)
+    own = i1 - i0 + 1
+    rest = nocc - 1 - i1
+    n_own = max(1, round(chunks * own / (own + rest)))
+    n_rest = max(1, chunks - n_own) if rest else 0
+    plan = []
+
+    def clip(lo, hi):
+        return max(lo, pb), min(hi, pe)
+
+    step = -(-own // n_own)
+    b = i1 + 1
     while b > i0:
         a = max(i0, b - step)
-        bounds.append((a, b))
+        # rows [a, i1] resident: pairs (i in [a, b), j in [i, i1])
+        plan.append((a, b, _merge([clip(pair_offset(i, nocc), pair_offset(i, nocc) + (i1 + 1 - i))
+                                   for i in range(a, b)])))
         b = a
-    return bounds
+    if rest:
+        step = -(-rest // n_rest)
+        a = i1 + 1
+        while a < nocc:
+            b = min(nocc, a + step)
+            plan.append((a, b, _merge([clip(pair_offset(i, nocc) + (a - i),
+                                            pair_offset(i, nocc) + (b - i))
+                                       for i in range(i0, i1 + 1)])))
+            a = b
+    return plan
 
 
-def chunk_pair_range(nocc: int, pb: int, pe: int, a: int, b: int) -> tuple[int, int]:
-    """Pair ids of [pb, pe) whose first row lies in [a, b): once rows a..nocc-1
-    are resident these pairs (i >= a, j >= i) have both their rows."""
-    lo = max(pb, pair_offset(a, nocc))
-    hi = min(pe, pair_offset(b, nocc) if b < nocc else nocc * (nocc + 1) // 2)
-    return lo, hi
+def _wide_rows_estimate(stats: list[float], naux: int) -> float:
+    """Relative energy error estimate of the three-digit fp32 path from
+    tt_mp2_range_stats_f32's sums (see include/trntensor_b200.h)."""
+    a2, a3, n = stats
+    if not n > 0.0:
+        return 0.0
+    return 2.0 * math.sqrt(max(0.0, 2.0**-47 * a2 * a3 / naux)) / (n * n / naux)
+
+
+# Above this estimate the fp32 energy is computed with the five-digit
+# (fp64-accurate) kernel instead of the three-digit one; Gaussian rows stay
+# well below it (1e-7 to 3e-7 at the benchmark sizes).
+WIDE_ROWS_MAX_EST = 1e-6
+
+
+def _range_stats(lib, X: torch.Tensor, rows: int, naux: int, stats: torch.Tensor, stream) -> None:
+    _lib.check(lib.tt_mp2_range_stats_f32(_ptr(X), rows, naux, _ptr(stats), stream),
+               "tt_mp2_range_stats_f32")
+
+
+def mp2_range_estimate(B: torch.Tensor) -> float:
+    """The wide-row error estimate of an fp32 B (nocc, nvir, naux), computed
+    on the current CUDA device; the fp32 energy uses five digits above
+    WIDE_ROWS_MAX_EST."""
+    lib = _lib.load()
+    dev = _device()
+    Bd = _to_dev(B, dev, torch.float32)
+    stats = torch.zeros(3, dtype=torch.float64, device=dev)
+    rows = int(B.shape[0]) * int(B.shape[1])
+    _range_stats(lib, Bd, rows, int(B.shape[2]), stats, ctypes.c_void_p(_stream_handle()))
+    return _wide_rows_estimate(stats.tolist(), int(B.shape[2]))
+
+
+def _needs_more_digits(stats: torch.Tensor, naux: int) -> bool:
+    """Host read of the range statistics (one synchronisation); False when
+    TRNTENSOR_B200_ASYNC asks for no host reads."""
+    if os.environ.get("TRNTENSOR_B200_ASYNC", "") in ("1", "true", "yes"):
+        return False
+    return _wide_rows_estimate(stats.tolist(), naux) > WIDE_ROWS_MAX_EST
 
 
 def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
     """fp32 DF-MP2 energy of host-resident pinned B with the copy overlapped.
 
-    Pairs (i, j), i <= j, with i >= a only need B rows a..nocc-1, and in
-    row-major pair order they form one contiguous id range. B is therefore
-    copied in row chunks from the last row backwards on a side stream; each
-    chunk is split into int8 slices as it lands (tt_split_i8_rows) and its
-    pair range is computed on the current stream while the next chunk is in
-    flight. Only the rows the pair range needs are copied.
+    Rows are copied on a side stream in the order of ``host_copy_plan``;
+    each chunk is split into int8 slices as it lands (tt_split_i8_rows) and
+    the pairs it completes run on the current stream while the next chunk is
+    in flight. Only the rows the pair range needs are copied. If the range
+    statistics of those rows call for more digits, the energy is recomputed
+    from the device copy with the five-digit kernel.
     """
     nocc, nvir, naux = (int(s) for s in B.shape)
     stream = torch.cuda.current_stream(dev)
@@ -283,13 +368,19 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
     qbytes = (3 * rows_total * pad + 255) // 256 * 256
     q_ptr = ws.data_ptr()
     s_ptr = ws.data_ptr() + qbytes
+    plan = host_copy_plan(nocc, pb, pe, chunks)
+    i0 = min(a for a, _, _ in plan)
     Bd = torch.empty((nocc, nvir, naux), dtype=torch.float32, device=dev)
-    bounds = host_row_chunks(nocc, pb, pe, chunks)
-    energies = torch.zeros(len(bounds), dtype=torch.float64, device=dev)
-    status = torch.zeros(len(bounds), dtype=torch.int32, device=dev)
+    if i0 > 0:
+        Bd[:i0].zero_()  # rows no pair of the range reads (keeps a recompute clean)
+    nlaunch = sum(len(r) for _, _, r in plan)
+    energies = torch.zeros(max(1, nlaunch), dtype=torch.float64, device=dev)
+    status = torch.zeros(max(1, nlaunch), dtype=torch.int32, device=dev)
+    stats = torch.zeros(3, dtype=torch.float64, device=dev)
     copy_stream = torch.cuda.Stream(dev)
     copy_stream.wait_stream(stream)  # Bd / ws allocations are ordered before the copies
-    for c, (a, b) in enumerate(bounds):
+    k = 0
+    for a, b, ranges in plan:
         with torch.cuda.stream(copy_stream):
             Bd[a:b].copy_(B[a:b], non_blocking=True)
             done = torch.cuda.Event()
@@ -298,13 +389,14 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
         _lib.check(lib.tt_split_i8_rows(ctypes.c_void_p(Bd.data_ptr()), ctypes.c_void_p(q_ptr),
                                         ctypes.c_void_p(s_ptr), a * nvir, (b - a) * nvir,
                                         rows_total, naux, pad, sp), "tt_split_i8_rows")
-        lo, hi = chunk_pair_range(nocc, pb, pe, a, b)
-        if hi > lo:
+        _range_stats(lib, Bd[a:b], (b - a) * nvir, naux, stats, sp)
+        for lo, hi in ranges:
             st = lib.tt_mp2_energy_presplit_i8(
                 ctypes.c_void_p(q_ptr), ctypes.c_void_p(s_ptr), pad, _ptr(eo), _ptr(ev), nocc,
-                nvir, lo, hi, ctypes.c_void_p(energies.data_ptr() + 8 * c), None,
-                ctypes.c_void_p(status.data_ptr() + 4 * c), sp)
+                nvir, lo, hi, ctypes.c_void_p(energies.data_ptr() + 8 * k), None,
+                ctypes.c_void_p(status.data_ptr() + 4 * k), sp)
             _lib.check(st, "tt_mp2_energy_presplit_i8")
+            k += 1
     Bd.record_stream(copy_stream)
     energy = energies.sum()
     if os.environ.get("TRNTENSOR_B200_ASYNC", "") not in ("1", "true", "yes"):
@@ -312,6 +404,9 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
         if bad.numel():
             raise _lib.DeviceError(f"tt_mp2_energy_presplit_i8: device wait ran out "
                                    f"(status 0x{int(status[bad[0, 0]].item()):x})")
+    if _needs_more_digits(stats, naux):
+        del ws
+        energy, _ = _cuda_mp2_energy(Bd, eo, ev, precision="kahan", pair_range=(pb, pe))
     return energy
 
 
