@@ -251,6 +251,42 @@ int tt_gemm_f32(const float* A, int a_kmajor, long long strideA, const float* B,
                 long long strideB, float* C, long long strideC, int M, int N, int K, int batch,
                 void* workspace, size_t workspace_bytes, int* dev_status, void* stream);
 
+/* ------------------------------------------------- double-double (dd) */
+
+/* Workspace of tt_mp2_energy_dd (per-block partial sums on this device). */
+size_t tt_mp2_dd_workspace_bytes(int nocc, int nvir, int naux);
+
+/*
+ * DF-MP2 energy in double-double arithmetic on CUDA cores
+ * (precision="dd": trntensor/einsum.py:112-116 names it, the reference
+ * raises NotImplementedError). fp64 inputs; every T_ab and T_ba is a Dot2
+ * dot product (sum and product errors collected, ~2^-106 relative for
+ * well-conditioned sums), energy terms in double-double add / multiply /
+ * divide, sums over (a, b), pairs and blocks in double-double, in a fixed
+ * order (deterministic). energy[0..1] = (hi, lo) of the sum over the
+ * unordered pairs [pair_begin, pair_end) with the weights of
+ * tt_mp2_energy_f32; pair_partials (nullable, nocc*nocc*2 doubles) receives
+ * each visited E_ij as (hi, lo) at [i][j] and [j][i], zero elsewhere.
+ * A correctness mode: about 20x the fp64 CUDA-core kernel's time.
+ */
+int tt_mp2_energy_dd(const double* B, const double* eps_occ, const double* eps_vir, int nocc,
+                     int nvir, int naux, long long pair_begin, long long pair_end,
+                     void* workspace, size_t workspace_bytes, double* energy,
+                     double* pair_partials, void* stream);
+
+/*
+ * Batched C[b] = A[b] . B[b] in double-double on CUDA cores: A and B given
+ * as hi parts plus optional (nullable) lo parts, so that double-double
+ * intermediates chain; C returned as hi and (nullable) lo. Layouts as in
+ * tt_gemm_f32 (a_kmajor / b_kmajor; C (M, N) row-major per batch, batch
+ * strides in elements). Serves precision="dd" for einsum contractions
+ * (trntensor/einsum.py:112-116) and the two AO->MO steps.
+ */
+int tt_gemm_dd(const double* A_hi, const double* A_lo, int a_kmajor, long long strideA,
+               const double* B_hi, const double* B_lo, int b_kmajor, long long strideB,
+               double* C_hi, double* C_lo, long long strideC, int M, int N, int K, int batch,
+               void* stream);
+
 /* Failure-detection check (no counterpart in the reference): one thread waits,
  * through the same bounded mbarrier wait every kernel here uses, on a phase
  * that nothing completes. After budget_cycles (at most the kernels' own

@@ -86,3 +86,51 @@ def ao_to_mo_two_step(eri, C_occ, C_vir, dtype=None):
 def ao_to_mo_fused(eri, C_occ, C_vir):
     """The reference's literal 3-operand contraction; small sizes only."""
     return np.einsum("mi,na,mnP->iaP", C_occ, C_vir, eri, optimize=False)
+
+
+# ------------------------------------------------ high-precision references
+# For precision="dd" (double-double) checks: the same sums in Python's
+# decimal arithmetic at 60 significant digits. Every float converts to
+# Decimal exactly; products, sums and quotients round at 1e-60 relative,
+# far below double-double's ~1e-32. Small sizes only (pure Python loops).
+
+def _dec(x):
+    from decimal import Decimal
+
+    return Decimal(float(x))
+
+
+def mp2_energy_decimal(B, eps_occ, eps_vir, prec=60):
+    """sum over ordered pairs of sum_ab T_ab (2 T_ab - T_ba) / D_ijab
+    (trntensor/quantum.py:87-100) in decimal arithmetic; returns a Decimal."""
+    from decimal import localcontext
+
+    B = np.asarray(B, dtype=np.float64)
+    nocc, nvir, naux = B.shape
+    with localcontext() as ctx:
+        ctx.prec = prec
+        Bd = [[[_dec(B[i, a, p]) for p in range(naux)] for a in range(nvir)] for i in range(nocc)]
+        eo = [_dec(v) for v in np.asarray(eps_occ, dtype=np.float64)]
+        ev = [_dec(v) for v in np.asarray(eps_vir, dtype=np.float64)]
+        total = _dec(0.0)
+        for i in range(nocc):
+            for j in range(nocc):
+                T = [[sum(x * y for x, y in zip(Bd[i][a], Bd[j][b])) for b in range(nvir)]
+                     for a in range(nvir)]
+                for a in range(nvir):
+                    for b in range(nvir):
+                        total += T[a][b] * (2 * T[a][b] - T[b][a]) / (eo[i] + eo[j] - ev[a] - ev[b])
+        return total
+
+
+def matmul_decimal(A, B, prec=60):
+    """A @ B (2-D) in decimal arithmetic; returns a nested list of Decimals."""
+    from decimal import localcontext
+
+    A = np.asarray(A, dtype=np.float64)
+    B = np.asarray(B, dtype=np.float64)
+    with localcontext() as ctx:
+        ctx.prec = prec
+        Ad = [[_dec(v) for v in row] for row in A]
+        Bt = [[_dec(B[k, n]) for k in range(B.shape[0])] for n in range(B.shape[1])]
+        return [[sum(x * y for x, y in zip(r, c)) for c in Bt] for r in Ad]

@@ -32,8 +32,9 @@ class TestMp2Validation:
         B3 = torch.randn(3, 4, 5)
         with pytest.raises(ValueError, match="precision must be"):
             tt.mp2_energy(B3, torch.randn(3), torch.randn(4), precision="bogus")
-        with pytest.raises(NotImplementedError, match="kahan"):
-            tt.mp2_energy(B3, torch.randn(3), torch.randn(4), precision="dd")
+        if not torch.cuda.is_available():  # "dd" runs on the GPU (no CPU path)
+            with pytest.raises(RuntimeError, match="CUDA"):
+                tt.mp2_energy(B3, torch.randn(3), torch.randn(4), precision="dd")
 
     def test_empty_is_zero(self):
         e = tt.mp2_energy(torch.randn(0, 4, 5), torch.randn(0), torch.randn(4))
@@ -130,8 +131,10 @@ class TestEinsum:
         r = tt.einsum("ij,jk->ik", a, b, precision="kahan")
         assert r.dtype == torch.float32
         torch.testing.assert_close(r, (a.double() @ b.double()).float())
-        with pytest.raises(NotImplementedError, match="kahan"):
-            tt.einsum("ij,jk->ik", a, b, precision="dd")
+        assert tt.plan_contraction("ij,jk->ik", a, b, precision="dd").precision == "dd"
+        if not torch.cuda.is_available():  # "dd" runs on the GPU (no CPU path)
+            with pytest.raises(RuntimeError, match="CUDA"):
+                tt.einsum("ij,jk->ik", a, b, precision="dd")
 
     def test_multi_einsum(self):
         B = torch.randn(3, 4, 5)

@@ -97,3 +97,13 @@ def test_config4_fixture_reproduces():
         got = float(oracle.mp2_pair_energy(Bij, eo[[i, j]], ev, 0, 1))
         assert got == pytest.approx(e, rel=1e-12)
         assert Bij[0].sum() == pytest.approx(fx["row_sums"][str(i)], rel=1e-12)
+
+
+def test_decimal_oracle_matches_fp64_golden(golden):
+    """The 60-digit decimal restatement (the precision="dd" checker) agrees
+    with the reference's fp64 energies on two known-answer cases."""
+    for name in ("kat_manual", "kat_public"):
+        B, eo, ev = mp2_case_inputs(golden, name)
+        e = float(oracle.mp2_energy_decimal(B.double().numpy(), eo.double().numpy(),
+                                            ev.double().numpy()))
+        assert e == pytest.approx(float(golden[f"{name}/e_fp64"]), rel=1e-13)

@@ -28,7 +28,13 @@ from .plan import (
     plan_cache_info,
     plan_contraction,
 )
-from .quantum import ao_to_mo_transform, df_mp2_energy, mp2_energy, mp2_pair_energies
+from .quantum import (
+    ao_to_mo_transform,
+    df_mp2_energy,
+    mp2_energy,
+    mp2_energy_dd,
+    mp2_pair_energies,
+)
 
 __all__ = [
     "einsum",
@@ -52,5 +58,6 @@ __all__ = [
     "mp2_energy",
     "ao_to_mo_transform",
     "mp2_pair_energies",
+    "mp2_energy_dd",
     "df_mp2_energy",
 ]

@@ -56,6 +56,9 @@ SIGNATURES: dict[str, tuple] = {
     "tt_ao2mo_f64": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P, _P]),
     "tt_ao2mo_f64_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "tt_ao2mo_f64_tc": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P, _P, _P]),
+    "tt_mp2_dd_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "tt_mp2_energy_dd": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _SZ, _P, _P, _P]),
+    "tt_gemm_dd": (_I, [_P, _P, _I, _LL, _P, _P, _I, _LL, _P, _P, _LL, _I, _I, _I, _I, _P]),
     "tt_debug_wait_timeout": (_I, [_P, _LL, _P, _P]),
     "tt_gemm_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "tt_gemm_f32": (_I, [_P, _I, _LL, _P, _I, _LL, _P, _LL, _I, _I, _I, _I, _P, _SZ, _P, _P]),

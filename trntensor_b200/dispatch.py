@@ -514,3 +514,87 @@ def _cuda_gemm(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     _lib.check(st, "tt_gemm_f32")
     _check_status(status, "tt_gemm_f32")
     return out
+
+
+# ------------------------------------------------------ double-double (dd)
+
+def _dd_dev(t: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    """fp64 copy on the device (exact for every float input dtype)."""
+    return _to_dev(t, dev, torch.float64)
+
+
+def _cuda_mp2_energy_dd(B, eps_occ, eps_vir, *, pair_range=None, return_partials=False):
+    """DF-MP2 energy in double-double (precision="dd").
+
+    Returns ``((2,) fp64 [hi, lo] device tensor, partials)`` where partials
+    is a (nocc, nocc, 2) fp64 tensor of per-pair (hi, lo) or None.
+    """
+    lib = _lib.load()
+    dev = _device()
+    nocc, nvir, naux = (int(s) for s in B.shape)
+    Bd, eo, ev = _dd_dev(B, dev), _dd_dev(eps_occ, dev), _dd_dev(eps_vir, dev)
+    npairs = nocc * (nocc + 1) // 2
+    pb, pe = (0, npairs) if pair_range is None else (int(pair_range[0]), int(pair_range[1]))
+    ws_bytes = int(lib.tt_mp2_dd_workspace_bytes(nocc, nvir, naux))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    energy = torch.empty(2, dtype=torch.float64, device=dev)
+    partials = (torch.empty((nocc, nocc, 2), dtype=torch.float64, device=dev)
+                if return_partials else None)
+    st = lib.tt_mp2_energy_dd(_ptr(Bd), _ptr(eo), _ptr(ev), nocc, nvir, naux, pb, pe, _ptr(ws),
+                              ws_bytes, _ptr(energy), _ptr(partials),
+                              ctypes.c_void_p(_stream_handle()))
+    _lib.check(st, "tt_mp2_energy_dd")
+    return energy, partials
+
+
+def _cuda_bmm_dd(A_hi, A_lo, B_hi, B_lo):
+    """Batched (b, M, K) x (b, K, N) in double-double; lo parts nullable.
+    All operands fp64 CUDA tensors; returns (C_hi, C_lo), each (b, M, N)."""
+    lib = _lib.load()
+    nb, M, K = (int(s) for s in A_hi.shape)
+    N = int(B_hi.shape[-1])
+    dev = A_hi.device
+    C_hi = torch.empty((nb, M, N), dtype=torch.float64, device=dev)
+    C_lo = torch.empty_like(C_hi)
+    if C_hi.numel() == 0:
+        return C_hi, C_lo
+    if K == 0:
+        return C_hi.zero_(), C_lo.zero_()
+    A_hi, B_hi = A_hi.contiguous(), B_hi.contiguous()
+    A_lo = None if A_lo is None else A_lo.contiguous()
+    B_lo = None if B_lo is None else B_lo.contiguous()
+    stream = ctypes.c_void_p(_stream_handle())
+    for b0 in range(0, nb, 65535):
+        b1 = min(nb, b0 + 65535)
+        st = lib.tt_gemm_dd(
+            _ptr(A_hi[b0:b1]), _ptr(None if A_lo is None else A_lo[b0:b1]), 1, M * K,
+            _ptr(B_hi[b0:b1]), _ptr(None if B_lo is None else B_lo[b0:b1]), 0, K * N,
+            _ptr(C_hi[b0:b1]), _ptr(C_lo[b0:b1]), M * N, M, N, K, b1 - b0, stream)
+        _lib.check(st, "tt_gemm_dd")
+    return C_hi, C_lo
+
+
+def _cuda_ao_to_mo_dd(eri, C_occ, C_vir):
+    """AO->MO transform in double-double: step 1 keeps the (i, n, P)
+    intermediate as (hi, lo) and step 2 reads both. Returns (B_hi, B_lo)."""
+    lib = _lib.load()
+    dev = _device()
+    nbf, _, naux = (int(s) for s in eri.shape)
+    nocc, nvir = int(C_occ.shape[1]), int(C_vir.shape[1])
+    e, co, cv = _dd_dev(eri, dev), _dd_dev(C_occ, dev), _dd_dev(C_vir, dev)
+    out_hi = torch.zeros((nocc, nvir, naux), dtype=torch.float64, device=dev)
+    out_lo = torch.zeros_like(out_hi)
+    if out_hi.numel() == 0 or nbf == 0:
+        return out_hi, out_lo
+    inter_hi = torch.empty((nocc, nbf, naux), dtype=torch.float64, device=dev)
+    inter_lo = torch.empty_like(inter_hi)
+    stream = ctypes.c_void_p(_stream_handle())
+    # step 1: inter[i, (n, P)] = sum_m C_occ[m, i] eri[m, (n, P)]
+    _lib.check(lib.tt_gemm_dd(_ptr(co), None, 0, 0, _ptr(e), None, 0, 0, _ptr(inter_hi),
+                              _ptr(inter_lo), nocc * nbf * naux, nocc, nbf * naux, nbf, 1,
+                              stream), "tt_gemm_dd")
+    # step 2: out[i] = C_vir^T inter[i] (batched over i, dd intermediate)
+    _lib.check(lib.tt_gemm_dd(_ptr(cv), None, 0, 0, _ptr(inter_hi), _ptr(inter_lo), 0,
+                              nbf * naux, _ptr(out_hi), _ptr(out_lo), nvir * naux, nvir, naux,
+                              nbf, nocc, stream), "tt_gemm_dd")
+    return out_hi, out_lo

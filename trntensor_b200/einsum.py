@@ -3,9 +3,10 @@
 Host-side Python like the reference (trntensor/einsum.py:51-241): optional
 dtype cast, planning through :mod:`trntensor_b200.plan`, cuTENSOR-style
 ``alpha``/``beta``/``out`` post-ops and the ``precision=`` semantics
-(``"kahan"`` = contract in fp64, cast back to the input dtype; ``"dd"``
-raises ``NotImplementedError``). Strategies execute with torch on the
-operands' device (cuBLAS for CUDA tensors).
+(``"kahan"`` = contract in fp64, cast back to the input dtype; ``"dd"`` =
+contract in double-double on the GPU, cast back to the input dtype).
+Strategies execute with torch on the operands' device (cuBLAS for CUDA
+tensors) unless ``set_backend("cuda")`` selects the tensor-core GEMM.
 """
 
 from __future__ import annotations
@@ -104,10 +105,8 @@ def _execute(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.T
         dt = operands[0].dtype if operands else torch.float32
         return torch.einsum(subscripts, *(op.to(torch.float64) for op in operands)).to(dt)
     if plan.precision == "dd":
-        raise NotImplementedError(
-            "precision='dd' (double-double accumulation) is not available; "
-            "use precision='kahan' (fp64 accumulation) as an alternative."
-        )
+        dt = operands[0].dtype if operands else torch.float32
+        return _einsum_dd(subscripts, operands, plan).to(device=operands[0].device, dtype=dt)
     if plan.strategy == "matmul":
         A, B = operands
         a, b = (A.T if plan.transA else A), (B.T if plan.transB else B)
@@ -157,6 +156,95 @@ def _execute_path(subscripts: str, operands: tuple, plan: ContractionPlan) -> to
         ops = [o for k, o in enumerate(ops) if k not in (x, y)] + [res]
         terms = [t for k, t in enumerate(terms) if k not in (x, y)] + [res_term]
     return ops[0]
+
+
+def _dd_reduce(hi, lo, term: str, keep: set):
+    """Sum a double-double operand over its indices not in ``keep`` (a
+    contraction with a ones vector, in double-double). Returns (hi, lo, term)."""
+    from .dispatch import _cuda_bmm_dd
+
+    drop = [c for c in term if c not in keep]
+    if not drop:
+        return hi, lo, term
+    rest = [c for c in term if c in keep]
+    perm = [term.index(c) for c in rest + drop]
+    shp = [hi.shape[term.index(c)] for c in rest]
+    k = 1
+    for c in drop:
+        k *= hi.shape[term.index(c)]
+    r = 1
+    for n in shp:
+        r *= n
+    h = hi.permute(perm).reshape(1, r, k)
+    l_ = None if lo is None else lo.permute(perm).reshape(1, r, k)
+    ones = torch.ones((1, k, 1), dtype=torch.float64, device=hi.device)
+    ch, cl = _cuda_bmm_dd(h, l_, ones, None)
+    return ch.reshape(shp), cl.reshape(shp), "".join(rest)
+
+
+def _dd_binary(a, b, ta: str, tb: str, out: str):
+    """One two-operand contraction in double-double as a batched GEMM:
+    (batch, left, k) x (batch, k, right) -> permuted to ``out``."""
+    from .dispatch import _cuda_bmm_dd
+
+    (ah, al), (bh, bl) = a, b
+    ah, al, ta = _dd_reduce(ah, al, ta, set(tb) | set(out))
+    bh, bl, tb = _dd_reduce(bh, bl, tb, set(ta) | set(out))
+    batch = [c for c in ta if c in tb and c in out]
+    contr = [c for c in ta if c in tb and c not in out]
+    left = [c for c in ta if c not in tb]
+    right = [c for c in tb if c not in ta]
+    size = {c: ah.shape[ta.index(c)] for c in ta}
+    size.update({c: bh.shape[tb.index(c)] for c in tb})
+
+    def prod(cs):
+        n = 1
+        for c in cs:
+            n *= size[c]
+        return n
+
+    pa = [ta.index(c) for c in batch + left + contr]
+    pb = [tb.index(c) for c in batch + contr + right]
+    shape_a = (prod(batch), prod(left), prod(contr))
+    shape_b = (prod(batch), prod(contr), prod(right))
+    A = ah.permute(pa).reshape(shape_a)
+    Al = None if al is None else al.permute(pa).reshape(shape_a)
+    Bm = bh.permute(pb).reshape(shape_b)
+    Bl = None if bl is None else bl.permute(pb).reshape(shape_b)
+    ch, cl = _cuda_bmm_dd(A, Al, Bm, Bl)
+    res_terms = batch + left + right
+    full = [size[c] for c in res_terms]
+    perm = [res_terms.index(c) for c in out]
+    return ch.reshape(full).permute(perm), cl.reshape(full).permute(perm)
+
+
+def _einsum_dd(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.Tensor:
+    """precision="dd": the contraction in double-double on the CUDA device
+    (host operands are moved there); every binary step is a double-double
+    GEMM (csrc/dd.cu) and intermediates keep their lo parts. Returns the hi
+    part (fp64); the caller casts to the input dtype."""
+    from .dispatch import _dd_dev, _device
+
+    lhs, out = _parse_subscripts(subscripts)
+    terms = lhs.split(",")
+    if any(len(set(t)) != len(t) for t in terms) or len(set(out)) != len(out):
+        raise NotImplementedError("precision='dd' does not support repeated indices in a term")
+    dev = next((op.device for op in operands if op.device.type == "cuda"), None) or _device()
+    ops = [(_dd_dev(op, dev), None) for op in operands]
+    if len(ops) == 1:
+        h, l_, t = _dd_reduce(ops[0][0], None, terms[0], set(out))
+        return h.permute([t.index(c) for c in out]) if out else h.reshape(())
+    steps = plan.contraction_path if len(ops) > 2 else [(0, 1)]
+    for n, (x, y) in enumerate(steps):
+        if n == len(steps) - 1:
+            res_term = out
+        else:
+            later = set(out).union(*(set(t) for k, t in enumerate(terms) if k not in (x, y)))
+            res_term = "".join(dict.fromkeys(c for c in terms[x] + terms[y] if c in later))
+        res = _dd_binary(ops[x], ops[y], terms[x], terms[y], res_term)
+        ops = [o for k, o in enumerate(ops) if k not in (x, y)] + [res]
+        terms = [t for k, t in enumerate(terms) if k not in (x, y)] + [res_term]
+    return ops[0][0]
 
 
 def multi_einsum(*contractions: tuple) -> list[torch.Tensor]:

@@ -58,11 +58,6 @@ def plan_cache_info() -> dict[str, int]:
 def _check_precision(precision: str) -> None:
     if precision not in _PRECISIONS:
         raise ValueError(f"precision must be 'fast', 'kahan', or 'dd', got {precision!r}")
-    if precision == "dd":
-        raise NotImplementedError(
-            "precision='dd' (double-double accumulation) is not available; "
-            "use precision='kahan' (fp64 accumulation) as an alternative."
-        )
 
 
 def _parse_subscripts(subscripts: str) -> tuple[str, str]:

@@ -5,8 +5,9 @@ Same signatures, validation and error messages as the reference
 keyword with ``trntensor.einsum``'s meaning (trntensor/einsum.py:108-116):
 ``"fast"`` computes in the input dtype (fp32-level accuracy from int8
 tensor-core GEMMs on three Ozaki digits per value, accumulated exactly),
-``"kahan"`` computes in fp64 and returns the input dtype, ``"dd"`` raises
-``NotImplementedError``.
+``"kahan"`` computes in fp64 and returns the input dtype, ``"dd"`` computes
+in double-double (about 106 bits; CUDA-core kernels, a correctness mode) and
+returns the input dtype (``mp2_energy_dd`` returns the hi and lo parts).
 
 Unlike the reference there is no backend gate and no CPU fallback: both
 functions always run the sm_100a kernels, moving host tensors to the current
@@ -17,7 +18,7 @@ from __future__ import annotations
 
 import torch
 
-from .dispatch import _cuda_mp2_energy
+from .dispatch import _cuda_mp2_energy, _cuda_mp2_energy_dd
 from .plan import _check_precision
 
 
@@ -53,7 +54,7 @@ def mp2_energy(
     B : (nocc, nvir, naux) tensor
     eps_occ : (nocc,) tensor
     eps_vir : (nvir,) tensor
-    precision : "fast" | "kahan"
+    precision : "fast" | "kahan" | "dd"
 
     Returns
     -------
@@ -63,8 +64,22 @@ def mp2_energy(
     nocc, nvir, _naux = B.shape
     if nocc == 0 or nvir == 0 or _naux == 0:
         return B.new_zeros(())
+    if precision == "dd":
+        energy, _ = _cuda_mp2_energy_dd(B, eps_occ, eps_vir)
+        return energy[0].to(device=B.device, dtype=B.dtype)
     energy, _ = _cuda_mp2_energy(B, eps_occ, eps_vir, precision=precision)
     return energy.to(device=B.device, dtype=B.dtype)
+
+
+def mp2_energy_dd(B: torch.Tensor, eps_occ: torch.Tensor, eps_vir: torch.Tensor) -> torch.Tensor:
+    """The DF-MP2 energy in double-double as a (2,) float64 tensor [hi, lo]
+    (E = hi + lo to about 2^-106 relative for well-conditioned sums), on
+    ``B``'s device. Same validation as ``mp2_energy``."""
+    _validate_mp2(B, eps_occ, eps_vir, "dd")
+    if B.numel() == 0:
+        return torch.zeros(2, dtype=torch.float64, device=B.device)
+    energy, _ = _cuda_mp2_energy_dd(B, eps_occ, eps_vir)
+    return energy.to(B.device)
 
 
 def mp2_pair_energies(
@@ -84,6 +99,9 @@ def mp2_pair_energies(
     nocc, nvir, naux = (int(x) for x in B.shape)
     if nocc == 0 or nvir == 0 or naux == 0:
         return torch.zeros((nocc, nocc), dtype=torch.float64, device=B.device)
+    if precision == "dd":
+        _, partials = _cuda_mp2_energy_dd(B, eps_occ, eps_vir, return_partials=True)
+        return partials[..., 0].contiguous().to(B.device)
     _, partials = _cuda_mp2_energy(B, eps_occ, eps_vir, precision=precision, return_partials=True)
     return partials.to(B.device)
 
@@ -114,8 +132,11 @@ def ao_to_mo_transform(
     if C_vir.dim() != 2 or C_vir.shape[0] != nbasis:
         raise ValueError(f"C_vir must have shape ({nbasis}, nvir); got {tuple(C_vir.shape)}")
     _check_precision(precision)
-    from .dispatch import _cuda_ao_to_mo_transform
+    from .dispatch import _cuda_ao_to_mo_dd, _cuda_ao_to_mo_transform
 
+    if precision == "dd":
+        hi, _ = _cuda_ao_to_mo_dd(eri, C_occ, C_vir)
+        return hi.to(device=eri.device, dtype=eri.dtype)
     out = _cuda_ao_to_mo_transform(eri, C_occ, C_vir, precision=precision)
     return out.to(device=eri.device, dtype=eri.dtype)
 
