@@ -420,11 +420,52 @@ def ao2mo_roofline(alg_bytes: float, flops: float, ms: float, naux_local: int) -
     return out
 
 
+def ao2mo_cpu_baseline(eri, co, cv, naux, w=16):
+    """The reference's AO->MO CPU form as its tests and benchmarks run it:
+    the two-step ``trntensor.einsum`` ("mi,mnP->inP" then "na,inP->iaP",
+    trntensor/einsum.py via the unmodified baseline/_ref install), timed on a
+    ``w``-wide aux slab (every aux column costs the same), median of 3,
+    extrapolated to all of naux. The numpy restatement in oracle/ stands in
+    without the install."""
+    e_c = eri[:, :, :w].cpu().contiguous()
+    co_c, cv_c = co.cpu(), cv.cpu()
+    kind = "reference"
+    ref = ROOT / "baseline" / "_ref"
+    try:
+        if str(ref) not in sys.path:
+            sys.path.insert(0, str(ref))
+        import trntensor as ref_tt
+
+        def run():
+            inter = ref_tt.einsum("mi,mnP->inP", co_c, e_c)
+            return ref_tt.einsum("na,inP->iaP", cv_c, inter)
+    except Exception:
+        from oracle import oracle
+
+        kind = "port"
+        e_np, co_np, cv_np = e_c.numpy(), co_c.numpy(), cv_c.numpy()
+
+        def run():
+            return oracle.ao_to_mo_two_step(e_np, co_np, cv_np)
+    run()
+    ts = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        run()
+        ts.append(time.perf_counter() - t0)
+    t_cpu = statistics.median(ts) * naux / w
+    info = cpu_info()
+    return {"ms": t_cpu * 1e3, "cores": info["torch_threads"], "kind": kind,
+            "sample": f"two-step trntensor.einsum on a {w}-wide aux slab (fp32), median of 3, "
+                      f"extrapolated x{naux / w:g}", **info}
+
+
 def measure_ao2mo(args, rank, world, local):
     """AO->MO config 3 transform time, aux index sharded over the ranks.
 
-    Each rank transforms its contiguous (nbf, nbf, naux/N) slab (sliced out
-    before timing), inputs resident; ms = max over ranks of the mean step.
+    Each rank transforms its (nbf, nbf, naux/N) aux slab, read in place from
+    the full resident eri (tt_ao2mo_f32_slab); ms = max over ranks of the
+    mean step.
     """
     from trntensor_b200 import _lib, distributed
     from trntensor_b200.inputs import ao2mo_inputs
@@ -435,19 +476,21 @@ def measure_ao2mo(args, rank, world, local):
     nbf, nocc, nvir, naux = c["nbf"], c["nocc"], c["nvir"], c["naux"]
     eri, co, cv = ao2mo_inputs(nbf, nocc, nvir, naux, seed=0, device=dev)
     p0, p1 = distributed.aux_slab(naux, rank, world)
-    slab = eri[:, :, p0:p1].contiguous()
     nl = p1 - p0
-    del eri
     out = torch.empty(nocc, nvir, nl, dtype=torch.float32, device=dev)
     ws_bytes = int(lib.tt_ao2mo_workspace_bytes(nbf, nocc, nvir, nl, 4))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     status = torch.zeros((), dtype=torch.int32, device=dev)
     sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    # the rank's aux columns are read in place from the full eri (strided
+    # slab); one GPU reads all of it
+    eri_at = ctypes.c_void_p(eri.data_ptr() + 4 * p0)
 
     def step():
-        _lib.check(lib.tt_ao2mo_f32(P(slab), P(co), P(cv), nbf, nocc, nvir, nl, P(ws), ws_bytes,
-                                    P(out), P(status), sp), "tt_ao2mo_f32")
+        _lib.check(lib.tt_ao2mo_f32_slab(eri_at, nbf * naux, naux, P(co), P(cv), nbf, nocc, nvir,
+                                         nl, P(ws), ws_bytes, P(out), P(status), sp),
+                   "tt_ao2mo_f32_slab")
 
     for _ in range(args.warmup):
         step()
@@ -470,20 +513,7 @@ def measure_ao2mo(args, rank, world, local):
            "kernels": "int8 Ozaki tcgen05 GEMMs (column-scaled slices), two steps"}
     res["roofline"] = ao2mo_roofline(alg_bytes / world, flops / world, ms, nl)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        import numpy as np
-
-        from oracle import oracle
-
-        w = 16
-        e_np = slab[:, :, :w].cpu().numpy()
-        co_np, cv_np = co.cpu().numpy(), cv.cpu().numpy()
-        oracle.ao_to_mo_two_step(e_np, co_np, cv_np)
-        t0 = time.perf_counter()
-        oracle.ao_to_mo_two_step(e_np, co_np, cv_np)
-        t_cpu = (time.perf_counter() - t0) * naux / w
-        res["cpu_baseline"] = {"ms": t_cpu * 1e3, "cores": _blas_threads(), "kind": "port",
-                               "sample": f"two-step einsum port on a {w}-wide aux slab (fp32), "
-                                         f"extrapolated x{naux // w}"}
+        res["cpu_baseline"] = ao2mo_cpu_baseline(eri, co, cv, naux)
     del ws, out
     torch.cuda.empty_cache()
     if rank == 0 and world == 1:
@@ -491,8 +521,8 @@ def measure_ao2mo(args, rank, world, local):
         # and the CUDA-core fp64 path, same inputs promoted to fp64
         from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
 
-        s64, co64, cv64 = slab.double(), co.double(), cv.double()
-        del slab
+        s64, co64, cv64 = eri.double(), co.double(), cv.double()
+        del eri
         torch.cuda.empty_cache()
 
         def t64(kernel, n):
@@ -515,7 +545,7 @@ def measure_ao2mo(args, rank, world, local):
                            float((o_tc - o_s).abs().max() / o_s.abs().max())}
         del s64, o_tc, o_s
     else:
-        del slab
+        del eri
     torch.cuda.empty_cache()
     return res
 

@@ -204,6 +204,23 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
                  int nvir, int naux, void* workspace, size_t workspace_bytes, float* B_out,
                  int* dev_status, void* stream);
 
+/*
+ * tt_ao2mo_f32 on a strided P-slab of a larger eri, without copying it: the
+ * rank's aux columns [p0, p0 + naux_local) of an (nbf, nbf, naux_total)
+ * tensor are passed as eri = base + p0 with ld_n = naux_total and
+ * ld_m = nbf * naux_total (elements); step 1 reads the slab through a 3-D
+ * tensor map. B_out is the compact (nocc, nvir, naux_local) block and the
+ * workspace is tt_ao2mo_workspace_bytes(nbf, nocc, nvir, naux_local, 4).
+ * Needs eri 16-byte aligned, ld_n and ld_m multiples of 4 (TT_ERR_ALIGN)
+ * and nbf > 128 (TT_ERR_SHAPE; the caller copies the slab then).
+ * The interface the multi-GPU aux split needs (each rank reads its P range
+ * in place); replaces the pad-and-copy at trntensor/nki/dispatch.py:286-336.
+ */
+int tt_ao2mo_f32_slab(const float* eri, long long ld_m, long long ld_n, const float* C_occ,
+                      const float* C_vir, int nbf, int nocc, int nvir, int naux_local,
+                      void* workspace, size_t workspace_bytes, float* B_out, int* dev_status,
+                      void* stream);
+
 /* Diagnostic: the same transform in plain fp32 on CUDA cores. */
 int tt_ao2mo_simt_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf,
                       int nocc, int nvir, int naux, void* workspace, size_t workspace_bytes,

@@ -52,6 +52,31 @@ def _worker(rank, world, port, mode, q):
             p0, p1 = distributed.aux_slab(naux, rank, world)
             full = distributed.gather_aux(B[:, :, p0:p1].contiguous(), naux)
             q.put((rank, bool(torch.equal(full, B)), True))
+        elif mode == "strided":
+            # each rank addresses its aux columns inside the full eri the way
+            # tt_ao2mo_f32_slab's 3-D tensor map does: base + p0, strides
+            # (nbf * naux, naux, 1), extents (nbf, nbf, p1 - p0)
+            nbf, naux = 5, 12
+            eri = torch.arange(nbf * nbf * naux, dtype=torch.float32).reshape(nbf, nbf, naux)
+            p0, p1 = distributed.aux_slab(naux, rank, world)
+            view = torch.as_strided(eri, (nbf, nbf, p1 - p0), (nbf * naux, naux, 1), p0)
+            ok = bool(torch.equal(view, eri[:, :, p0:p1]))
+            full = distributed.gather_aux(view.contiguous(), naux)
+            q.put((rank, ok and bool(torch.equal(full, eri)), True))
+        elif mode == "pipeline":
+            # every rank copies rows in host_copy_plan order and runs the pair
+            # ranges each step lists; each pair id contributes (id + 1) once
+            from trntensor_b200.dispatch import host_copy_plan
+
+            nocc = 23
+            npairs = nocc * (nocc + 1) // 2
+            b, e = distributed.pair_range(npairs, rank, world)
+            local = torch.zeros((), dtype=torch.float64)
+            for _, _, ranges in host_copy_plan(nocc, b, e, chunks=5):
+                for lo, hi in ranges:
+                    local += float(sum(range(lo + 1, hi + 1)))
+            distributed.reduce_energy(local)
+            q.put((rank, local.item(), npairs * (npairs + 1) / 2))
         elif mode == "fail":
             if rank == 1:
                 raise RuntimeError("injected failure on rank 1 before the all-reduce")
@@ -87,6 +112,14 @@ def _run(world, mode):
 @pytest.mark.parametrize("world", [2, 4])
 def test_energy_all_reduce(world):
     for rank, got, want in _run(world, "reduce"):
+        assert got == want, (rank, got)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_strided_slabs_and_pipelined_pairs(world):
+    for rank, ok, want in _run(world, "strided"):
+        assert ok is want, (rank, ok)
+    for rank, got, want in _run(world, "pipeline"):
         assert got == want, (rank, got)
 
 

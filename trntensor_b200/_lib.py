@@ -52,6 +52,7 @@ SIGNATURES: dict[str, tuple] = {
     "tt_mp2_energy_simt_f32": (_I, [_P, _P, _P, _I, _I, _I, _LL, _LL, _P, _P, _P]),
     "tt_ao2mo_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "tt_ao2mo_f32": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P, _P, _P]),
+    "tt_ao2mo_f32_slab": (_I, [_P, _LL, _LL, _P, _P, _I, _I, _I, _I, _P, _SZ, _P, _P, _P]),
     "tt_ao2mo_simt_f32": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P, _P]),
     "tt_ao2mo_f64": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P, _P]),
     "tt_ao2mo_f64_workspace_bytes": (_SZ, [_I, _I, _I, _I]),

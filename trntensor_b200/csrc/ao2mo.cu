@@ -268,9 +268,13 @@ size_t tt_ao2mo_workspace_bytes(int nbf, int nocc, int nvir, int naux, int elem_
   return 0;
 }
 
-int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf, int nocc,
-                 int nvir, int naux, void* workspace, size_t workspace_bytes, float* B_out,
-                 int* dev_status, void* stream) {
+// ld_m / ld_n: eri strides (elements) of its m and n indices; a contiguous
+// eri has ld_n = naux, ld_m = nbf * naux. slab: eri is a strided P-slab
+// (ld_n > naux possible), read through a 3-D tensor map by the fused step 1.
+static int ao2mo_f32_impl(const float* eri, long long ld_m, long long ld_n, bool slab,
+                          const float* C_occ, const float* C_vir, int nbf, int nocc, int nvir,
+                          int naux, void* workspace, size_t workspace_bytes, float* B_out,
+                          int* dev_status, void* stream) {
   using namespace tt;
   if (!eri || !C_occ || !C_vir || !workspace || !B_out || !dev_status) return TT_ERR_NULL;
   if (nbf <= 0 || nocc <= 0 || nvir <= 0 || naux <= 0) return TT_ERR_SHAPE;
@@ -301,7 +305,15 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
             pa = (int)pad16(naux);
   const long long ncol = (long long)nbf * naux;
   const char* pre = std::getenv("TRNTENSOR_B200_AO2MO_PRESLICE");
-  const bool preslice = (pre != nullptr && pre[0] == '1') || (ncol % 4 != 0) || !aligned16(eri);
+  const bool preslice =
+      !slab && ((pre != nullptr && pre[0] == '1') || (ncol % 4 != 0) || !aligned16(eri));
+  if (slab) {
+    // the fused on-chip split (its own column scales) is the only slab reader
+    const int istages = 2;
+    if ((nbf + ozc::kKC - 1) / ozc::kKC < istages + 1) return TT_ERR_SHAPE;
+    if (!aligned16(eri) || ld_n % 4 != 0 || ld_m % 4 != 0) return TT_ERR_ALIGN;
+    if (ld_n < naux || ld_m < ld_n * nbf) return TT_ERR_SHAPE;
+  }
   // Column-scaled int8 slices of C_occ and C_vir. For the on-chip path C_occ's
   // slices are written kARep times (batch stride 0 on the source): every CTA
   // re-reads them for each tile, and spreading those reads over several copies
@@ -328,7 +340,8 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     // (ozaki_gemm_cvt.cuh); with fewer, a separate column-max pass runs.
     const char* cm = std::getenv("TRNTENSOR_B200_AO2MO_COLMAX");
     const int nkc = (nbf + ozc::kKC - 1) / ozc::kKC;
-    const bool fuse = nkc >= istages + 1 && !(cm != nullptr && cm[0] == '1');
+    const bool fuse = slab || (nkc >= istages + 1 && !(cm != nullptr && cm[0] == '1'));
+    if (slab && nkc < istages + 1) return TT_ERR_SHAPE;
     // Split-K over CTA pairs: each half needs as many k-chunks.
     const char* sk = std::getenv("TRNTENSOR_B200_AO2MO_SPLITK");
     const bool split = fuse && nkc / 2 >= istages + 1 && g_split_clusters[dev] > 0 &&
@@ -343,9 +356,16 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     const uint64_t xd[2] = {(uint64_t)ncol, (uint64_t)nbf};
     const uint64_t xs[1] = {(uint64_t)ncol * 4};
     const uint32_t xb[2] = {(uint32_t)ozc::kTile, (uint32_t)ozc::kKC};
-    if (slice_map(&ma, qo, po, nbf, ozc::kARep) ||
-        encode_tmap(&mx, eri, 2, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (slice_map(&ma, qo, po, nbf, ozc::kARep)) return TT_ERR_TMA;
+    if (slab) {
+      // (P, n, m) with strides ld_n, ld_m; box 128 P x 1 n x 64 m
+      const uint64_t sd[3] = {(uint64_t)naux, (uint64_t)nbf, (uint64_t)nbf};
+      const uint64_t ss[2] = {(uint64_t)ld_n * 4, (uint64_t)ld_m * 4};
+      const uint32_t sb[3] = {(uint32_t)ozc::kTile, 1u, (uint32_t)ozc::kKC};
+      if (encode_tmap(&mx, eri, 3, sd, ss, sb, CU_TENSOR_MAP_SWIZZLE_NONE)) return TT_ERR_TMA;
+    } else if (encode_tmap(&mx, eri, 2, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_NONE)) {
       return TT_ERR_TMA;
+    }
     ozc::Params pc;
     pc.sA = so;
     pc.sX = se;
@@ -355,7 +375,9 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
     pc.N = nbf * naux;
     pc.K = nbf;
     pc.tiles_m = (nocc + ozc::kTile - 1) / ozc::kTile;
-    pc.tiles_n = (int)((ncol + ozc::kTile - 1) / ozc::kTile);
+    pc.slab_p = slab ? naux : 0;
+    pc.tiles_p = (naux + ozc::kTile - 1) / ozc::kTile;
+    pc.tiles_n = slab ? nbf * pc.tiles_p : (int)((ncol + ozc::kTile - 1) / ozc::kTile);
     pc.err = dev_status;
 #ifdef TT_OZC_PROFILE
     pc.prof = g_ozc_prof;
@@ -391,6 +413,21 @@ int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int n
   // step 2: B_out[i][a][P] = sum_n C_vir[n][a] inter[i][n][P]
   return oz_gemm(qv, sv, pv, 1, qi, si, pa, nocc, nvir, naux, nbf, B_out, naux,
                  (long long)nvir * naux, dev_status, s, sms);
+}
+
+int tt_ao2mo_f32(const float* eri, const float* C_occ, const float* C_vir, int nbf, int nocc,
+                 int nvir, int naux, void* workspace, size_t workspace_bytes, float* B_out,
+                 int* dev_status, void* stream) {
+  return ao2mo_f32_impl(eri, (long long)nbf * naux, naux, false, C_occ, C_vir, nbf, nocc, nvir,
+                        naux, workspace, workspace_bytes, B_out, dev_status, stream);
+}
+
+int tt_ao2mo_f32_slab(const float* eri, long long ld_m, long long ld_n, const float* C_occ,
+                      const float* C_vir, int nbf, int nocc, int nvir, int naux_local,
+                      void* workspace, size_t workspace_bytes, float* B_out, int* dev_status,
+                      void* stream) {
+  return ao2mo_f32_impl(eri, ld_m, ld_n, true, C_occ, C_vir, nbf, nocc, nvir, naux_local,
+                        workspace, workspace_bytes, B_out, dev_status, stream);
 }
 
 size_t tt_ao2mo_f64_workspace_bytes(int nbf, int nocc, int nvir, int naux) {

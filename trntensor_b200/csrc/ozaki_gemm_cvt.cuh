@@ -90,6 +90,12 @@ struct Params {
   long long* prof;  // optional per-CTA wait-cycle counters (TT_OZC_PROFILE builds)
   int l2hint;       // kFuse: keep max-pass lines in L2 (evict_last) for the conversion
                     // re-read, which marks them evict_first; output stores streaming
+  // P-slab mode (slab_p > 0, kFuse only): X is a strided (m, n, P) view with
+  // slab_p aux columns per n row, read through a 3-D tensor map; a column
+  // tile is 128 aux columns of one n (tiles_p per n row). The output stays
+  // compact: column n * slab_p + P.
+  int slab_p;
+  int tiles_p;
 };
 
 // 16-byte store to a shared::cluster address (another CTA's shared memory).
@@ -207,9 +213,20 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Output column base n0 of tile w (and its row tile m0). Consecutive tiles
+  // share the X columns.
   auto tile_of = [&](long long w, int& m0, int& n0) {
-    n0 = (int)(w / p.tiles_m) * kTile;  // consecutive tiles share the X columns
+    const long long ct = w / p.tiles_m;
     m0 = (int)(w % p.tiles_m) * kTile;
+    if (p.slab_p)
+      n0 = (int)((ct / p.tiles_p) * p.slab_p + (ct % p.tiles_p) * kTile);
+    else
+      n0 = (int)ct * kTile;
+  };
+  // Valid output columns of the tile at column base n0.
+  auto cols_of = [&](int n0) -> int {
+    const int left = p.slab_p ? p.slab_p - n0 % p.slab_p : p.N - n0;
+    return left < kTile ? left : kTile;
   };
 
   if (warp == 0 || warp == kAWarp) {
@@ -246,7 +263,14 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
 #endif
         if (fp32) {
           mbar_arrive_expect_tx(&fill_bar[s], kFBytes);
-          if (kFuse && p.l2hint)
+          if (p.slab_p) {  // box {128 P, 1 n, 64 m} of the strided slab
+            const int n = n0 / p.slab_p, p0 = n0 % p.slab_p;
+            if (kFuse && p.l2hint)
+              tma_load_3d_hint(fring + s * kFBytes, &mapX, &fill_bar[s], p0, n, kc * kKC,
+                               max_pass ? keep : drop);
+            else
+              tma_load_3d(fring + s * kFBytes, &mapX, &fill_bar[s], p0, n, kc * kKC);
+          } else if (kFuse && p.l2hint)
             tma_load_2d_hint(fring + s * kFBytes, &mapX, &fill_bar[s], n0, kc * kKC,
                              max_pass ? keep : drop);
           else
@@ -357,7 +381,8 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
     const int half = ew >> 2;  // this warp's block of kEpiCols columns
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+    const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                     (p.slab_p % 4 == 0);
     uint32_t round = 0;
     for (long long w = w0; w < n_tiles; w += wstep, ++round) {
       int m0, n0;
@@ -376,7 +401,7 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
       tc_fence_after();
       const int m = m0 + row;
       const float sa = m < p.M ? __ldg(p.sA + m) : 0.f;
-      const int nn = p.N - n0 < kTile ? p.N - n0 : kTile;
+      const int nn = cols_of(n0);
       // combine this thread's 64 columns and park them as fp32
 #pragma unroll
       for (int c = half * kEpiCols; c < (half + 1) * kEpiCols; c += 16) {

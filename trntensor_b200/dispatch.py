@@ -467,6 +467,34 @@ def _cuda_ao_to_mo_transform(
     return out
 
 
+def _cuda_ao_to_mo_slab(eri: torch.Tensor, C_occ: torch.Tensor, C_vir: torch.Tensor, p0: int,
+                        p1: int) -> torch.Tensor:
+    """fp32 AO->MO transform of eri's aux columns [p0, p1) read in place
+    (tt_ao2mo_f32_slab); eri is the full contiguous (nbf, nbf, naux) CUDA
+    fp32 tensor. Falls back to a slab copy where the strided read does not
+    apply (nbf <= 128, unaligned columns)."""
+    lib = _lib.load()
+    dev = eri.device
+    nbf, _, naux = (int(s) for s in eri.shape)
+    nocc, nvir, nl = int(C_occ.shape[1]), int(C_vir.shape[1]), p1 - p0
+    ok = (eri.is_cuda and eri.dtype == torch.float32 and eri.is_contiguous() and nbf > 128
+          and p0 % 4 == 0 and naux % 4 == 0 and nl > 0 and nocc * nvir > 0)
+    if not ok:
+        return _cuda_ao_to_mo_transform(eri[:, :, p0:p1], C_occ, C_vir)
+    co = _to_dev(C_occ, dev, torch.float32)
+    cv = _to_dev(C_vir, dev, torch.float32)
+    out = torch.empty((nocc, nvir, nl), dtype=torch.float32, device=dev)
+    ws_bytes = int(lib.tt_ao2mo_workspace_bytes(nbf, nocc, nvir, nl, 4))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    status = torch.empty((), dtype=torch.int32, device=dev)
+    st = lib.tt_ao2mo_f32_slab(ctypes.c_void_p(eri.data_ptr() + 4 * p0), nbf * naux, naux,
+                               _ptr(co), _ptr(cv), nbf, nocc, nvir, nl, _ptr(ws), ws_bytes,
+                               _ptr(out), _ptr(status), ctypes.c_void_p(_stream_handle()))
+    _lib.check(st, "tt_ao2mo_f32_slab")
+    _check_status(status, "tt_ao2mo_f32_slab")
+    return out
+
+
 def _operand_layout(X: torch.Tensor, kmajor_if_contiguous: bool):
     """(storage tensor, kmajor) for a 2-D/3-D operand without copying if possible."""
     if X.is_contiguous():

@@ -98,13 +98,20 @@ def ao_to_mo_transform(
     already the rank's contiguous slab. Returns the rank's (nocc, nvir, p1-p0)
     block of B. There is no communication.
     """
+    from .dispatch import _cuda_ao_to_mo_slab
     from .quantum import ao_to_mo_transform as _single
 
     rank, world = _world(group)
-    if not sharded_input:
-        p0, p1 = aux_slab(int(eri.shape[2]), rank, world)
-        eri = eri[:, :, p0:p1].contiguous()
-    return _single(eri, C_occ, C_vir, precision=precision)
+    if sharded_input:
+        return _single(eri, C_occ, C_vir, precision=precision)
+    p0, p1 = aux_slab(int(eri.shape[2]), rank, world)
+    if precision == "fast" and eri.is_cuda and eri.dtype == torch.float32:
+        # the rank's aux columns are read in place (strided 3-D tensor map)
+        from .quantum import _validate_ao2mo
+
+        _validate_ao2mo(eri, C_occ, C_vir, precision)
+        return _cuda_ao_to_mo_slab(eri, C_occ, C_vir, p0, p1)
+    return _single(eri[:, :, p0:p1], C_occ, C_vir, precision=precision)
 
 
 def gather_aux(local: torch.Tensor, naux: int, group=None) -> torch.Tensor:

@@ -106,19 +106,8 @@ def mp2_pair_energies(
     return partials.to(B.device)
 
 
-def ao_to_mo_transform(
-    eri: torch.Tensor,
-    C_occ: torch.Tensor,
-    C_vir: torch.Tensor,
-    *,
-    precision: str = "fast",
-) -> torch.Tensor:
-    """AO→MO transform B[i,a,P] = Σ_{μν} C_occ[μ,i] C_vir[ν,a] eri[μ,ν,P].
-
-    Two tensor-core GEMM phases ('mi,mnP->inP' then 'na,inP->iaP') with the
-    (i, ν, P) intermediate in an HBM workspace, as the reference's kernel does
-    (trntensor/nki/_kernels.py:209-296).
-    """
+def _validate_ao2mo(eri, C_occ, C_vir, precision):
+    """Checks and messages of trntensor/quantum.py:138-151, plus ``precision``."""
     if eri.dim() != 3:
         raise ValueError(f"eri must be 3D (nbasis, nbasis, naux); got shape {tuple(eri.shape)}")
     nbasis_mu, nbasis_nu, _naux = eri.shape
@@ -132,6 +121,22 @@ def ao_to_mo_transform(
     if C_vir.dim() != 2 or C_vir.shape[0] != nbasis:
         raise ValueError(f"C_vir must have shape ({nbasis}, nvir); got {tuple(C_vir.shape)}")
     _check_precision(precision)
+
+
+def ao_to_mo_transform(
+    eri: torch.Tensor,
+    C_occ: torch.Tensor,
+    C_vir: torch.Tensor,
+    *,
+    precision: str = "fast",
+) -> torch.Tensor:
+    """AO→MO transform B[i,a,P] = Σ_{μν} C_occ[μ,i] C_vir[ν,a] eri[μ,ν,P].
+
+    Two tensor-core GEMM phases ('mi,mnP->inP' then 'na,inP->iaP') with the
+    (i, ν, P) intermediate in an HBM workspace, as the reference's kernel does
+    (trntensor/nki/_kernels.py:209-296).
+    """
+    _validate_ao2mo(eri, C_occ, C_vir, precision)
     from .dispatch import _cuda_ao_to_mo_dd, _cuda_ao_to_mo_transform
 
     if precision == "dd":
