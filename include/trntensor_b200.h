@@ -137,7 +137,9 @@ int tt_mp2_energy_tf32x3(const float* B_hi, const float* B_lo, int naux_pad,
  * No counterpart in the reference. Computes the full energy (all pairs)
  * using a fixed scratch array inside the library instead of a workspace:
  * problems with tt_mp2_workspace_bytes(nocc, nvir, naux) >
- * TT_MP2_NOALLOC_SCRATCH_BYTES are rejected with TT_ERR_WORKSPACE. Calls no
+ * TT_MP2_NOALLOC_SCRATCH_BYTES are rejected with TT_ERR_WORKSPACE, and, as
+ * for tt_mp2_energy_f32, naux padded to 64 must not exceed 65535
+ * (TT_ERR_SHAPE even when the slices would fit the scratch). Calls no
  * allocation routine. All calls share the one scratch array: calls that
  * overlap on the GPU (other streams, other host threads) race and must be
  * serialised by the caller. The first call on a device looks up the

@@ -58,6 +58,26 @@ def test_noalloc_matches_workspace_entry_point(cuda_ok):
         assert abs(e.item() - ref) <= RTOL_F32 * abs(ref)
 
 
+def test_noalloc_leaves_device_memory_unchanged(cuda_ok):
+    """After one warm-up call (which may load the kernels' code), a further
+    call changes the device's free memory by nothing: no allocation routine
+    runs inside it."""
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    B, eo, ev = (t.cuda() for t in mp2_inputs(6, 200, 150, seed=23))
+    e = torch.empty((), dtype=torch.float64, device="cuda")
+    st = torch.empty((), dtype=torch.int32, device="cuda")
+    args = (_p(B), _p(eo), _p(ev), 6, 200, 150, _p(e), None, _p(st), stream)
+    assert lib.tt_mp2_energy_f32_noalloc(*args) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    assert lib.tt_mp2_energy_f32_noalloc(*args) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert st.item() == 0
+
+
 def test_noalloc_rejects_oversize(cuda_ok):
     lib = _lib.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)

@@ -43,8 +43,8 @@ using oz::level_combine;
 
 // Ring depths (template parameters of the kernel): kFStages fp32 landing
 // slots (TMA -> converters) and kIStages int8 slots (A by TMA, B by the
-// converters -> MMA). The default is 3 + 2; 2 + 3 (a deeper int8 ring in the
-// same shared memory) is built too and selected by TRNTENSOR_B200_AO2MO_RING=23.
+// converters -> MMA). 3 + 2 and 2 + 3 (a deeper int8 ring in the same shared
+// memory) are both built; TRNTENSOR_B200_AO2MO_RING=23 selects the latter.
 // The fused column scales need more k-chunks per CTA than int8 slots (the
 // scale double buffer is rewritten only after the MMA has started the next
 // tile, which a converter can only know from an int8 slot of that tile):
@@ -183,7 +183,7 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFStages; ++s) {
       mbar_init(&fullF[s], 1);
-      mbar_init(&freeF[s], kCvtWarps);
+      mbar_init(&freeF[s], 32 * kCvtWarps);
     }
     for (int s = 0; s < kIStages; ++s) {
       mbar_init(&fullA[s], 1);
@@ -500,9 +500,19 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
 #endif
       return ok;
     };
+    // Releasing a landing slot is a write-after-read hand-off across proxies:
+    // the converters read the slot with generic shared-memory loads, and the
+    // producer's next TMA (the async proxy) rewrites it. An mbarrier
+    // release/acquire chain orders generic accesses only, so every converter
+    // thread first fences its own reads against the async proxy
+    // (fence.proxy.async) and then arrives itself. Without the fence, about
+    // one transform in 300 read a slot that the next TMA had already begun
+    // to overwrite: the column maxima of a few columns (scales off by a power
+    // of two, results off in the last bits) or the digits of an 8-column
+    // group came from the following chunk.
     auto release_f = [&]() {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&freeF[itF % kFStages]);
+      fence_proxy_async_smem();
+      mbar_arrive(&freeF[itF % kFStages]);
       ++itF;
     };
     // One fp32 chunk of the next tile's strip folded into the column maxima.
@@ -587,9 +597,9 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
         ++itI;
         if (!wait_f()) continue;  // error: run on without waiting, to the next group_all
         const float4* src = reinterpret_cast<const float4*>(fring + (itF % kFStages) * kFBytes);
-        // Split this warp's rows into registers first: the byte permutes
-        // consume every loaded value, so once all lanes are past them (the
-        // __syncwarp) no read of the slot is outstanding and it can be refilled.
+        // Split this warp's rows into registers first, then release the
+        // slot (each thread fences and arrives for its own loads), so that
+        // the producer can refill it while the digits wait for an int8 slot.
         uint32_t q[kRows][3];
 #pragma unroll
         for (int j = 0; j < kRows; ++j) {
