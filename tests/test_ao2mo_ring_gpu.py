@@ -1,11 +1,14 @@
-"""AO->MO step 1 ring protocol: the 2 fp32 + 3 int8 slot ring
-(TRNTENSOR_B200_AO2MO_RING=23) and the default 3 + 2 ring produce
-bit-identical tensors, run after run. The arithmetic does not depend on the
-ring depth (same digits, same k order, same epilogue and split-K order), so
-any difference is a hand-off bug between producers, converters, the MMA
-thread and the epilogue. Config 1 (no fused scales: nbf = 128 is two
-k-chunks) and a 2-GB config-3 slab (nbf 1024, naux 512; fused scales and
-split-K over CTA pairs) each run 200 times."""
+"""AO->MO step 1 hand-off protocols: every form of the step-1 kernel gives
+the same tensor run after run. The forms are the default (column maxima
+from the max warps' global loads, one CTA per tile), the same split over a
+CTA pair, and the landing-ring forms with 3 fp32 + 2 int8 slots and with
+2 + 3 slots (TRNTENSOR_B200_AO2MO_GMAX=0, RING=32/23). Within one form the
+arithmetic is fixed (same digits, same k order, same epilogue and split-K
+order), so any difference between runs is a hand-off bug between
+producers, converters, max warps, the MMA thread and the epilogue; the two
+ring depths run the same arithmetic and must also agree with each other.
+Config 1 (no fused scales: nbf = 128 is two k-chunks) and a 2-GB config-3
+slab (nbf 1024, naux 512) run 200 times per form."""
 
 from __future__ import annotations
 
@@ -18,22 +21,33 @@ from trntensor_b200.inputs import ao2mo_inputs
 pytestmark = pytest.mark.gpu
 
 REPEATS = 200
+FORMS = {
+    "gmax": {},
+    "gmax_split": {"TRNTENSOR_B200_AO2MO_SPLITK": "1"},
+    "ring32": {"TRNTENSOR_B200_AO2MO_GMAX": "0", "TRNTENSOR_B200_AO2MO_RING": "32"},
+    "ring23": {"TRNTENSOR_B200_AO2MO_GMAX": "0", "TRNTENSOR_B200_AO2MO_RING": "23"},
+}
+ENV = ("TRNTENSOR_B200_AO2MO_SPLITK", "TRNTENSOR_B200_AO2MO_GMAX", "TRNTENSOR_B200_AO2MO_RING")
 
 
 @pytest.mark.parametrize("shape", [(128, 16, 112, 384), (1024, 128, 896, 512)])
-def test_ring_depths_bitwise_identical(cuda_ok, shape, monkeypatch):
+def test_step1_forms_bitwise_stable(cuda_ok, shape, monkeypatch):
     nbf, nocc, nvir, naux = shape
     eri, co, cv = ao2mo_inputs(nbf, nocc, nvir, naux, seed=21, device="cuda")
-    monkeypatch.delenv("TRNTENSOR_B200_AO2MO_RING", raising=False)
-    ref = _cuda_ao_to_mo_transform(eri, co, cv)
     ref64 = _cuda_ao_to_mo_transform(eri.double(), co.double(), cv.double())
-    err = ((ref.double() - ref64).abs().max() / ref64.abs().max()).item()
-    assert err <= 1e-5
-    del ref64
-    for ring in ("32", "23"):
-        monkeypatch.setenv("TRNTENSOR_B200_AO2MO_RING", ring)
+    refs = {}
+    for form, env in FORMS.items():
+        for k in ENV:
+            monkeypatch.delenv(k, raising=False)
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        ref = _cuda_ao_to_mo_transform(eri, co, cv)
+        err = ((ref.double() - ref64).abs().max() / ref64.abs().max()).item()
+        assert err <= 1e-5, form
         bad = 0
         for _ in range(REPEATS):
             out = _cuda_ao_to_mo_transform(eri, co, cv)
             bad += int(not torch.equal(out, ref))
-        assert bad == 0, f"ring {ring}: {bad} of {REPEATS} runs differ"
+        assert bad == 0, f"{form}: {bad} of {REPEATS} runs differ"
+        refs[form] = ref
+    assert torch.equal(refs["ring32"], refs["ring23"])

@@ -14,6 +14,7 @@ std::once_flag g_flags[kMaxDevices];
 int g_ok[kMaxDevices];
 int g_sms[kMaxDevices];
 int g_split_clusters[kMaxDevices];  // co-resident 2-CTA clusters of gemm_cvt_split_kernel
+int g_gmax_clusters[kMaxDevices];   // the same for gemm_cvt_gmax_split_kernel
 
 int setup(int dev) {
   return once_per_device(g_flags, g_ok, dev, [dev]() -> int {
@@ -56,6 +57,19 @@ int setup(int dev) {
           cudaSuccess)
         return TT_ERR_CUDA;
       g_split_clusters[dev] = n < n23 ? n : n23;
+      const int smg = ozc::smem_bytes(3, 2, true);
+      if (cudaFuncSetAttribute(ozc::gemm_cvt_gmax_split_kernel<3, 2>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, smg) != cudaSuccess ||
+          cudaFuncSetAttribute(ozc::gemm_cvt_gmax_kernel<3, 2>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, smg) != cudaSuccess)
+        return TT_ERR_CUDA;
+      cfg.blockDim = dim3(ozc::kThreadsG, 1, 1);
+      cfg.dynamicSmemBytes = smg;
+      int ng = 0;
+      if (cudaOccupancyMaxActiveClusters(&ng, ozc::gemm_cvt_gmax_split_kernel<3, 2>, &cfg) !=
+          cudaSuccess)
+        return TT_ERR_CUDA;
+      g_gmax_clusters[dev] = ng;
     }
     if (cudaFuncSetAttribute(oz64::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              oz64::kSmemBytes) != cudaSuccess)
@@ -386,11 +400,27 @@ static int ao2mo_f32_impl(const float* eri, long long ld_m, long long ld_n, bool
 #endif
     const char* hint = std::getenv("TRNTENSOR_B200_AO2MO_L2HINT");
     pc.l2hint = !(hint != nullptr && hint[0] == '0');  // on unless set to 0
+    pc.X = eri;
+    pc.ldx_m = slab ? ld_m : ncol;
+    pc.ldx_n = slab ? ld_n : 0;
+    // Column maxima from the max warps' global loads (default; 3 + 2 ring,
+    // one CTA per tile unless TRNTENSOR_B200_AO2MO_SPLITK=1) or through the
+    // landing ring (TRNTENSOR_B200_AO2MO_GMAX=0).
+    const char* gm = std::getenv("TRNTENSOR_B200_AO2MO_GMAX");
+    const bool gmax = fuse && !ring23 && !(gm != nullptr && gm[0] == '0');
+    const bool gsplit = gmax && split && sk != nullptr && sk[0] == '1' && g_gmax_clusters[dev] > 0;
     const long long tiles = (long long)pc.tiles_m * pc.tiles_n;
     const int grid = (int)(tiles < sms ? tiles : sms);
     const int smem = ozc::smem_bytes(ring23 ? 2 : 3, istages);
     const long long cl = tiles < g_split_clusters[dev] ? tiles : g_split_clusters[dev];
-    if (ring23) {
+    if (gmax) {
+      const int smg = ozc::smem_bytes(3, 2, true);
+      const long long cg = tiles < g_gmax_clusters[dev] ? tiles : g_gmax_clusters[dev];
+      if (gsplit)
+        ozc::gemm_cvt_gmax_split_kernel<3, 2><<<(int)(2 * cg), ozc::kThreadsG, smg, s>>>(ma, mx, pc);
+      else
+        ozc::gemm_cvt_gmax_kernel<3, 2><<<grid, ozc::kThreadsG, smg, s>>>(ma, mx, pc);
+    } else if (ring23) {
       if (split)
         ozc::gemm_cvt_split_kernel<2, 3><<<(int)(2 * cl), ozc::kThreads, smem, s>>>(ma, mx, pc);
       else if (fuse)

@@ -65,19 +65,36 @@ constexpr int kCvtWarps = TT_OZC_CVT_WARPS;  // 8 or 16: divides the 64 rows of 
 constexpr int kEpiCols = kTile * 4 / kEpiWarps;  // columns of one epilogue warp
 constexpr int kAWarp = 2 + kEpiWarps + kCvtWarps;  // A-slice producer (its own warp)
 constexpr int kThreads = 32 * (kAWarp + 1);
+// kGMax: the column maxima of the next tile come from kMaxWarps extra warps
+// that read the strip with plain global loads into registers, so that it
+// passes through neither the TMA landing ring nor shared memory, and the
+// converters only convert. The landing ring then carries each chunk once.
+#ifndef TT_OZC_MAX_WARPS
+#define TT_OZC_MAX_WARPS 8
+#endif
+#ifndef TT_OZC_MAX_UNROLL
+#define TT_OZC_MAX_UNROLL 8
+#endif
+constexpr int kMaxWarps = TT_OZC_MAX_WARPS;
+constexpr int kMaxUnroll = TT_OZC_MAX_UNROLL;  // rows in flight per lane of a max warp
+constexpr int kThreadsG = kThreads + 32 * kMaxWarps;
+constexpr int kMaxBar = 3;     // named barrier of the max warps
 constexpr int kQCols = 16;                    // output staged 16 columns at a time
 constexpr int kQLd = kQCols + 4;
 constexpr int kColPark = 3 * kTile;           // TMEM columns of the parked fp32 tile
 constexpr int kARep = 8;                      // copies of the A slices (CTA b reads copy b % kARep)
 constexpr int kOutBytes = kTile * kQLd * 4;
 constexpr int kCMaxBytes = kCvtWarps * kTile * 4;  // per-warp column maxima (fused scales)
-constexpr int smem_bytes(int fstages, int istages) {
+constexpr int kGMaxBytes = kMaxWarps * kTile * 4 + 2 * kTile * 4;  // kGMax: per-warp maxima, inv x 2
+constexpr int smem_bytes(int fstages, int istages, bool gmax = false) {
   return fstages * kFBytes + istages * kIBytes + kOutBytes + 2 * kTile * 4 + kCMaxBytes +
-         2 * kTile * 4 + 1024 + 256;
+         2 * kTile * 4 + (gmax ? kGMaxBytes : 0) + 1024 + 256;
 }
 constexpr int kSmemBytes = smem_bytes(kFStagesDefault, kIStagesDefault);
 static_assert(smem_bytes(2, 3) <= 232448, "2 + 3 ring exceeds shared memory");
+static_assert(smem_bytes(3, 2, true) <= 232448, "max-warp buffers exceed shared memory");
 constexpr int kCvtBar = 2;  // named barrier of the converter warps
+constexpr int kProfSlots = 12;  // per-CTA counters of TT_OZC_PROFILE builds
 
 struct Params {
   const float* sA;    // column scales of A (per m)
@@ -96,7 +113,23 @@ struct Params {
   // compact: column n * slab_p + P.
   int slab_p;
   int tiles_p;
+  // kGMax: X itself for the max warps' loads. Element (k, column n0 + c) of
+  // a tile is X[k * ldx_m + col_off(n0) + c], col_off(n0) = n0 (dense) or
+  // (n0 / slab_p) * ldx_n + n0 % slab_p (P-slab).
+  const float* X;
+  long long ldx_m;
+  long long ldx_n;
 };
+
+// 16-byte read-only global load with an L2 eviction-priority policy, not
+// allocated in L1 (each line is read once per pass).
+__device__ __forceinline__ float4 ldg_nc_hint_v4(const float* src, uint64_t policy) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(src), "l"(policy));
+  return v;
+}
 
 // 16-byte store to a shared::cluster address (another CTA's shared memory).
 __device__ __forceinline__ void st_cluster_v4(uint32_t addr, const float (&v)[4]) {
@@ -143,7 +176,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 // stores its partial tile, then rank 1 adds its own with red.global.add
 // (out_ready / out_done order the two and keep the barriers' phases apart).
 // C = (rank 0 partial) + (rank 1 partial): one fp32 rounding, deterministic.
-template <bool kFuse, bool kSplit, int kFStages, int kIStages>
+template <bool kFuse, bool kSplit, bool kGMax, int kFStages, int kIStages>
 __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUtensorMap& mapX,
                                               const Params& p) {
   extern __shared__ uint8_t smem_raw[];
@@ -166,7 +199,14 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
   uint64_t* pfull = scale_full + 2;      // [2] kSplit: the peer's column maxima have landed
   uint64_t* out_ready = pfull + 2;       // kSplit, rank 1: rank 0 has stored the tile
   uint64_t* out_done = out_ready + 1;    // kSplit, rank 0: rank 1 has added its partial
-  uint32_t* tmem_slot = (uint32_t*)(out_done + 1);
+  uint64_t* scale_free = out_done + 1;   // [2] kGMax: scales of a tile read by epilogue + converters
+  uint64_t* cvt_took = scale_free + 2;   // [2] kGMax: the converters have taken a tile's scales
+  uint32_t* tmem_slot = (uint32_t*)(cvt_took + 2);
+  // kGMax: per-warp column maxima of the max warps, [kMaxWarps][kTile], and
+  // the converters' 2^16 / s_n, [2][kTile] (after the barriers' 256 bytes)
+  float* gcmax = (float*)(smem + kFStages * kFBytes + kIStages * kIBytes + kOutBytes +
+                          2 * kTile * 4 + kCMaxBytes + 2 * kTile * 4 + 256);
+  float* einv = gcmax + kMaxWarps * kTile;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long n_tiles = (long long)p.tiles_m * p.tiles_n;
@@ -199,6 +239,10 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
     mbar_init(&pfull[1], 32);
     mbar_init(out_ready, 32 * kEpiWarps);
     mbar_init(out_done, 32 * kEpiWarps);
+    mbar_init(&scale_free[0], 32 * (kEpiWarps + kCvtWarps));
+    mbar_init(&scale_free[1], 32 * (kEpiWarps + kCvtWarps));
+    mbar_init(&cvt_took[0], 32 * kCvtWarps);
+    mbar_init(&cvt_took[1], 32 * kCvtWarps);
     fence_mbar_init();
     tma_prefetch_desc(&mapA);
     tma_prefetch_desc(&mapX);
@@ -284,20 +328,22 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
       // fused scales: the fp32 stream is the first tile's strip (maxima), then
       // per tile the chunks of the next tile's strip (maxima) interleaved with
       // the current tile's (conversion), in the order the converters take them
-      if (kFuse && fp32 && w0 < n_tiles)
+      // (kGMax: the max warps read the strips themselves; the ring carries
+      // only the conversion chunks)
+      if (kFuse && !kGMax && fp32 && w0 < n_tiles)
         for (int kc = k_lo; kc < k_hi; ++kc) issue(w0, kc, true);
       for (long long w = w0; w < n_tiles && ok; w += wstep) {
         const long long nxt = w + wstep;
         for (int kc = k_lo; kc < k_hi; ++kc) {
           issue(w, kc, false);
-          if (kFuse && fp32 && nxt < n_tiles) issue(nxt, kc, true);
+          if (kFuse && !kGMax && fp32 && nxt < n_tiles) issue(nxt, kc, true);
         }
       }
       const uint32_t issued = it;
       for (uint32_t k = (issued > (uint32_t)nst ? issued - nst : 0); k < issued; ++k)
         mbar_wait_drain(&fill_bar[k % nst], (k / nst) & 1u);
 #ifdef TT_OZC_PROFILE
-      if (p.prof) p.prof[blockIdx.x * 8 + (fp32 ? 6 : 7)] = w_prod;
+      if (p.prof) p.prof[blockIdx.x * kProfSlots + (fp32 ? 6 : 7)] = w_prod;
 #endif
     }
   } else if (warp == 1) {
@@ -367,10 +413,10 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
       mbar_wait_drain(final_bar, 0);
 #ifdef TT_OZC_PROFILE
       if (p.prof) {
-        p.prof[blockIdx.x * 8 + 0] = clock64() - t_begin;
-        p.prof[blockIdx.x * 8 + 1] = w_acc;
-        p.prof[blockIdx.x * 8 + 2] = w_a;
-        p.prof[blockIdx.x * 8 + 3] = w_c;
+        p.prof[blockIdx.x * kProfSlots + 0] = clock64() - t_begin;
+        p.prof[blockIdx.x * kProfSlots + 1] = w_acc;
+        p.prof[blockIdx.x * kProfSlots + 2] = w_a;
+        p.prof[blockIdx.x * kProfSlots + 3] = w_c;
       }
 #endif
     }
@@ -418,6 +464,7 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(acc_empty);  // levels drained: the next tile's MMAs may start
+      if (kGMax) mbar_arrive(&scale_free[round & 1u]);  // esc read
       // kSplit, rank 1: add onto rank 0's stored partial, so wait for it
       const bool adder = kSplit && rank == 1;
       if (adder && !group_all<32 * kEpiWarps, 1>(
@@ -477,6 +524,124 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
         }
       }
     }
+  } else if (kGMax && warp > kAWarp) {
+    // ------------------------------------------------------------ max warps
+    // Per tile of this CTA, in order: the column maxima of its K range (each
+    // lane owns four columns; warp mw reads rows mw, mw + kMaxWarps, ... with
+    // kMaxUnroll rows in flight), then the tile's scales. They run at most
+    // two tiles ahead of the converters and the epilogue (scale_free).
+    const int mw = warp - kAWarp - 1;
+    const uint64_t pol = p.l2hint ? l2_policy_evict_last() : l2_policy_evict_first();
+    const int kb = k_lo * kKC, ke = (k_hi * kKC < p.K) ? k_hi * kKC : p.K;
+    uint32_t round = 0;
+    bool ok = true;
+#ifdef TT_OZC_PROFILE
+    long long w_load = 0, w_free = 0, w_lead = 0;
+#endif
+    for (long long w = w0; w < n_tiles && ok; w += wstep, ++round) {
+      int m0, n0;
+      tile_of(w, m0, n0);
+      const uint32_t par = round & 1u;
+      const int nn = cols_of(n0);
+      const int c0 = 4 * lane;
+      const long long coff =
+          p.slab_p ? (long long)(n0 / p.slab_p) * p.ldx_n + n0 % p.slab_p : (long long)n0;
+      const float* col = p.X + coff + c0;
+      float mx[4] = {0.f, 0.f, 0.f, 0.f};
+      // Read tile r's strip only once the converters have begun tile r - 1,
+      // so that a CTA keeps about one strip between its two reads of it and
+      // the conversion's re-read still finds it in L2.
+#ifdef TT_OZC_PROFILE
+      const long long tt0 = clock64();
+#endif
+      if (round > 0 && !mbar_wait(&cvt_took[par ^ 1u], ((round - 1) >> 1) & 1u, p.err, kDevTimeoutFull))
+        ok = false;
+      if (!group_all<32 * kMaxWarps, kMaxBar>(ok)) break;
+#ifdef TT_OZC_PROFILE
+      w_lead += clock64() - tt0;
+      const long long tl = clock64();
+#endif
+      if (c0 + 3 < nn) {
+        int k = kb + mw;
+        for (; k + (kMaxUnroll - 1) * kMaxWarps < ke; k += kMaxUnroll * kMaxWarps) {
+          float4 v[kMaxUnroll];
+#pragma unroll
+          for (int u = 0; u < kMaxUnroll; ++u)
+            v[u] = ldg_nc_hint_v4(col + (long long)(k + u * kMaxWarps) * p.ldx_m, pol);
+#pragma unroll
+          for (int u = 0; u < kMaxUnroll; ++u) {
+            mx[0] = ozd::absmax(mx[0], v[u].x);
+            mx[1] = ozd::absmax(mx[1], v[u].y);
+            mx[2] = ozd::absmax(mx[2], v[u].z);
+            mx[3] = ozd::absmax(mx[3], v[u].w);
+          }
+        }
+        for (; k < ke; k += kMaxWarps) {
+          const float4 v = ldg_nc_hint_v4(col + (long long)k * p.ldx_m, pol);
+          mx[0] = ozd::absmax(mx[0], v.x);
+          mx[1] = ozd::absmax(mx[1], v.y);
+          mx[2] = ozd::absmax(mx[2], v.z);
+          mx[3] = ozd::absmax(mx[3], v.w);
+        }
+      } else {
+        // ragged last columns (the TMA tile reads zeros there)
+        for (int k = kb + mw; k < ke; k += kMaxWarps)
+          for (int j = 0; j < 4; ++j)
+            if (c0 + j < nn) mx[j] = ozd::absmax(mx[j], __ldg(col + (long long)k * p.ldx_m + j));
+      }
+#ifdef TT_OZC_PROFILE
+      w_load += clock64() - tl;
+#endif
+      reinterpret_cast<float4*>(gcmax)[mw * 32 + lane] = make_float4(mx[0], mx[1], mx[2], mx[3]);
+      group_sync<32 * kMaxWarps, kMaxBar>();
+      if (mw == 0) {
+        float mm[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          mm[k] = 0.f;
+#pragma unroll
+          for (int v = 0; v < kMaxWarps; ++v) mm[k] = fmaxf(mm[k], gcmax[v * kTile + c0 + k]);
+        }
+        if (kSplit) {
+          // Same exchange as the ring form: this warp alone reads pmax, in
+          // program order before it arrives on the peer's pfull for the next
+          // tile, so the peer's write of pmax[par] two tiles later cannot
+          // overtake these reads.
+          st_cluster_v4(mapa(smem_u32(pmax + par * kTile + c0), peer), mm);
+          mbar_arrive_cluster(mapa(smem_u32(&pfull[par]), peer));
+          ok = mbar_wait_cluster(&pfull[par], (round >> 1) & 1u, p.err, kDevTimeoutFull);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mm[k] = fmaxf(mm[k], pmax[par * kTile + c0 + k]);
+        }
+        // the epilogue and the converters are done with the scales of the
+        // tile two rounds back, which used this buffer
+#ifdef TT_OZC_PROFILE
+        const long long tf = clock64();
+#endif
+        if (ok) ok = mbar_wait(&scale_free[par], ((round >> 1) & 1u) ^ 1u, p.err, kDevTimeoutEmpty);
+#ifdef TT_OZC_PROFILE
+        w_free += clock64() - tf;
+#endif
+        if (ok) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float sc = ozd::scale_for_max(mm[k]);
+            escale[par * kTile + c0 + k] = sc;
+            einv[par * kTile + c0 + k] = ozd::inv_scale(sc);
+          }
+          mbar_arrive(&scale_full[par]);
+        }
+      }
+      // (the next tile's gcmax writes wait here until warp 0 has read it)
+      if (!group_all<32 * kMaxWarps, kMaxBar>(ok)) break;
+    }
+#ifdef TT_OZC_PROFILE
+    if (p.prof && mw == 0 && lane == 0) {
+      p.prof[blockIdx.x * kProfSlots + 8] = w_load;
+      p.prof[blockIdx.x * kProfSlots + 9] = w_free;
+      p.prof[blockIdx.x * kProfSlots + 11] = w_lead;
+    }
+#endif
   } else if (warp < kAWarp) {
     // ----------------------------------------------------------- converters
     const int cw = warp - (2 + kEpiWarps);
@@ -484,7 +649,7 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
     uint32_t itF = 0, itI = 0;  // fp32 ring and int8 ring positions
     bool ok = true;
 #ifdef TT_OZC_PROFILE
-    long long w_f = 0, w_e = 0;
+    long long w_f = 0, w_e = 0, w_s = 0;
 #endif
     float inv[4];  // 2^16 / s_n of this lane's four columns of the current tile
     float mx[4];   // running |max| of the same columns of the next tile (kFuse)
@@ -572,7 +737,7 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
     // (and writes the scales of tile r + 2 into escale[r & 1]) has waited for
     // an int8 slot that the MMA freed inside tile r + 1, so the epilogue has
     // already read escale[r & 1] and waited on scale_full[r & 1] for tile r.
-    if (kFuse && w0 < n_tiles) {
+    if (kFuse && !kGMax && w0 < n_tiles) {
       mx[0] = mx[1] = mx[2] = mx[3] = 0.f;
       for (int kc = 0; kc < nkl; ++kc) max_chunk();
       if (!finish_scales(0)) ok = false;
@@ -581,8 +746,24 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
     for (long long w = w0; w < n_tiles && ok; w += wstep, ++round) {
       int m0, n0;
       tile_of(w, m0, n0);
-      const bool next = kFuse && w + wstep < n_tiles;
-      if (!kFuse) {
+      const bool next = kFuse && !kGMax && w + wstep < n_tiles;
+      if (kGMax) {
+        const uint32_t par = round & 1u;
+#ifdef TT_OZC_PROFILE
+        const long long ts = clock64();
+#endif
+        if (!mbar_wait(&scale_full[par], (round >> 1) & 1u, p.err, kDevTimeoutFull)) {
+          ok = false;
+          break;
+        }
+#ifdef TT_OZC_PROFILE
+        w_s += clock64() - ts;
+#endif
+#pragma unroll
+        for (int k = 0; k < 4; ++k) inv[k] = einv[par * kTile + 4 * lane + k];
+        mbar_arrive(&scale_free[par]);
+        mbar_arrive(&cvt_took[par]);
+      } else if (!kFuse) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int n = n0 + 4 * lane + k;
@@ -640,8 +821,9 @@ __device__ __forceinline__ void gemm_cvt_body(const CUtensorMap& mapA, const CUt
     }
 #ifdef TT_OZC_PROFILE
     if (p.prof && cw == 0 && lane == 0) {
-      p.prof[blockIdx.x * 8 + 4] = w_f;
-      p.prof[blockIdx.x * 8 + 5] = w_e;
+      p.prof[blockIdx.x * kProfSlots + 4] = w_f;
+      p.prof[blockIdx.x * kProfSlots + 5] = w_e;
+      p.prof[blockIdx.x * kProfSlots + 10] = w_s;
     }
 #endif
   }
@@ -659,14 +841,30 @@ template <bool kFuse, int kFStages = kFStagesDefault, int kIStages = kIStagesDef
 static __global__ void __launch_bounds__(kThreads, 1)
     gemm_cvt_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX,
                     Params p) {
-  gemm_cvt_body<kFuse, false, kFStages, kIStages>(mapA, mapX, p);
+  gemm_cvt_body<kFuse, false, false, kFStages, kIStages>(mapA, mapX, p);
 }
 
 template <int kFStages = kFStagesDefault, int kIStages = kIStagesDefault>
 static __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_cvt_split_kernel(const __grid_constant__ CUtensorMap mapA,
                           const __grid_constant__ CUtensorMap mapX, Params p) {
-  gemm_cvt_body<true, true, kFStages, kIStages>(mapA, mapX, p);
+  gemm_cvt_body<true, true, false, kFStages, kIStages>(mapA, mapX, p);
+}
+
+// Fused scales from the max warps (kGMax): one CTA per tile, or split K over
+// a cluster of two CTAs (the pair exchanges maxima and partial tiles through
+// distributed shared memory, so that form needs the cluster launch).
+template <int kFStages, int kIStages>
+static __global__ void __launch_bounds__(kThreadsG, 1)
+    gemm_cvt_gmax_kernel(const __grid_constant__ CUtensorMap mapA,
+                         const __grid_constant__ CUtensorMap mapX, Params p) {
+  gemm_cvt_body<true, false, true, kFStages, kIStages>(mapA, mapX, p);
+}
+template <int kFStages, int kIStages>
+static __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
+    gemm_cvt_gmax_split_kernel(const __grid_constant__ CUtensorMap mapA,
+                               const __grid_constant__ CUtensorMap mapX, Params p) {
+  gemm_cvt_body<true, true, true, kFStages, kIStages>(mapA, mapX, p);
 }
 
 }  // namespace ozc
