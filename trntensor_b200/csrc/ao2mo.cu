@@ -109,8 +109,15 @@ int split_cols(const float* X, long long ldx, long long bsx, int batch, int K, i
   const long long nblk = (long long)batch * ((npad + oz::kSplitCols - 1) / oz::kSplitCols);
   const long long cap = (long long)sms * 8;
   const int grid = (int)(nblk < cap ? nblk : cap);
-  oz::colmax_kernel<<<grid, oz::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S);
-  oz::slice_kernel<<<grid, oz::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S, Q);
+  // One read of X (colmax_slice_kernel) unless TRNTENSOR_B200_SPLIT_TWOPASS=1.
+  const char* tp = std::getenv("TRNTENSOR_B200_SPLIT_TWOPASS");
+  if (tp != nullptr && tp[0] == '1') {
+    oz::colmax_kernel<<<grid, oz::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S);
+    oz::slice_kernel<<<grid, oz::kSplitThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S, Q);
+  } else {
+    const int g1 = (int)(nblk < sms ? nblk : sms);
+    oz::colmax_slice_kernel<<<g1, oz::kFusedThreads, 0, s>>>(X, ldx, bsx, batch, K, N, npad, S, Q);
+  }
   return cuda_status(cudaGetLastError());
 }
 

@@ -341,5 +341,107 @@ static __global__ void __launch_bounds__(kSplitThreads, 3)
   }
 }
 
+// One-read column split: colmax + slice fused per 128-column block. The
+// block's first pass (column maxima) reads its K x 128 strip from HBM with
+// an L2 evict_last policy; the second pass (slices) re-reads it from L2 with
+// evict_first, so X crosses HBM once instead of twice. One 1024-thread CTA
+// per SM keeps the strips in flight at sms x K x 512 B (76 MB at K = 1024,
+// inside the 126 MB L2); each warp keeps kFusedRows 16-byte loads in flight.
+// Bit-identical to colmax_kernel + slice_kernel.
+constexpr int kFusedThreads = 1024;
+constexpr int kFusedRows = 4;
+
+__device__ __forceinline__ void load4_hint(const float* xc, bool vec, int nvalid, float (&v)[4],
+                                           uint64_t pol) {
+  if (vec && nvalid >= 4) {
+    float4 f;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
+                 : "l"(xc), "l"(pol));
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = j < nvalid ? __ldg(xc + j) : 0.f;
+  }
+}
+
+static __global__ void __launch_bounds__(kFusedThreads, 1)
+    colmax_slice_kernel(const float* __restrict__ X, long long ldx, long long bsx, int batch,
+                        int K, int N, int npad, float* __restrict__ S, int8_t* __restrict__ Q) {
+  constexpr int kWarps = kFusedThreads / 32;
+  __shared__ float red[kWarps][kSplitCols];
+  __shared__ float sinv[kSplitCols];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int ncb = (npad + kSplitCols - 1) / kSplitCols;
+  const long long plane = (long long)batch * K * npad;
+  const bool vec = (ldx % 4 == 0) && (bsx % 4 == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
+  const uint64_t keep = l2_policy_evict_last(), drop = l2_policy_evict_first();
+  for (long long blk = blockIdx.x; blk < (long long)batch * ncb; blk += gridDim.x) {
+    const int b = (int)(blk / ncb);
+    const int nb = (int)(blk % ncb) * kSplitCols;
+    const int n = nb + lane * 4;
+    const int nvalid = N - n;
+    const float* xc = X + b * bsx + n;
+    // pass 1: column maxima
+    float mx[4] = {0.f, 0.f, 0.f, 0.f};
+    if (nvalid > 0) {
+      for (int k0 = wp; k0 < K; k0 += kWarps * kFusedRows) {
+        float v[kFusedRows][4];
+#pragma unroll
+        for (int r = 0; r < kFusedRows; ++r) {
+          const int k = k0 + r * kWarps;
+          if (k < K) load4_hint(xc + (long long)k * ldx, vec, nvalid, v[r], keep);
+          else v[r][0] = v[r][1] = v[r][2] = v[r][3] = 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < kFusedRows; ++r)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mx[j] = ozd::absmax(mx[j], v[r][j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[wp][lane * 4 + j] = mx[j];
+    __syncthreads();
+    if (threadIdx.x < kSplitCols) {
+      float m = 0.f;
+#pragma unroll 8
+      for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[w][threadIdx.x]);
+      const int nn = nb + threadIdx.x;
+      const float sc = nn < N ? scale_for_max(m) : 0.f;
+      if (nn < npad) S[(long long)b * npad + nn] = sc;
+      sinv[threadIdx.x] = ozd::inv_scale(sc);
+    }
+    __syncthreads();
+    // pass 2: slices, the strip re-read from L2
+    if (n < npad) {
+      float inv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) inv[j] = sinv[lane * 4 + j];
+      int8_t* q1 = Q + (long long)b * K * npad + n;
+      for (int k0 = wp; k0 < K; k0 += kWarps * kFusedRows) {
+        float v[kFusedRows][4];
+#pragma unroll
+        for (int r = 0; r < kFusedRows; ++r) {
+          const int k = k0 + r * kWarps;
+          if (k < K && nvalid > 0) load4_hint(xc + (long long)k * ldx, vec, nvalid, v[r], drop);
+          else v[r][0] = v[r][1] = v[r][2] = v[r][3] = 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < kFusedRows; ++r) {
+          const int k = k0 + r * kWarps;
+          if (k >= K) break;
+          uint32_t w1, w2, w3;
+          ozd::split4(v[r], inv, w1, w2, w3);
+          const long long o = (long long)k * npad;
+          *reinterpret_cast<uint32_t*>(q1 + o) = w1;
+          *reinterpret_cast<uint32_t*>(q1 + o + plane) = w2;
+          *reinterpret_cast<uint32_t*>(q1 + o + 2 * plane) = w3;
+        }
+      }
+    }
+    __syncthreads();  // red / sinv free for the next block
+  }
+}
+
 }  // namespace oz
 }  // namespace tt
