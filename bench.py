@@ -382,8 +382,8 @@ AO_CONFIG = dict(nbf=1024, nocc=128, nvir=896, naux=3072)
 # DRAM bytes (read + write) of one transform per aux index at config 3's
 # nbf / nocc / nvir, summed over its kernels: ncu dram__bytes_read.sum +
 # dram__bytes_write.sum of one call at naux 512 (the traffic grows with naux:
-# every kernel works per aux column), divided by 512.
-AO_TRAFFIC_BYTES_PER_AUX = None
+# every kernel works per aux column), divided by 512: 3662.3 MB / 512.
+AO_TRAFFIC_BYTES_PER_AUX = 7.153e6
 
 
 def int8_peak_from_driver(peaks: dict) -> tuple[float, str]:

@@ -254,3 +254,16 @@ def test_strided_p_slab_matches_contiguous(cuda_ok, shape, world):
         parts.append(got)
     full = torch.cat(parts, dim=2).cpu().numpy()
     assert max_rel(full, ref64) <= TOL_F32
+
+
+def test_one_read_split_matches_two_pass(cuda_ok, monkeypatch):
+    """The one-read column split (max pass, then slices re-read from L2)
+    produces the same scales and digits as the two-pass kernels, so the
+    transforms agree bit for bit (ragged column blocks included)."""
+    from trntensor_b200.dispatch import _cuda_ao_to_mo_transform
+    eri, co, cv = ao2mo_inputs(300, 130, 70, 50, seed=5, device="cuda")
+    monkeypatch.delenv("TRNTENSOR_B200_SPLIT_TWOPASS", raising=False)
+    one = _cuda_ao_to_mo_transform(eri, co, cv)
+    monkeypatch.setenv("TRNTENSOR_B200_SPLIT_TWOPASS", "1")
+    two = _cuda_ao_to_mo_transform(eri, co, cv)
+    assert torch.equal(one, two)
