@@ -280,3 +280,26 @@ def test_greedy_path_avoids_outer_products():
     A, B, C = torch.randn(5, 3), torch.randn(4, 3), torch.randn(5, 4, 6)
     torch.testing.assert_close(tt.einsum("mi,na,mnP->iaP", A, B, C),
                                torch.einsum("mi,na,mnP->iaP", A, B, C))
+
+
+def test_einsum_product_orders_match_torch():
+    """Every index order of a matmul- or bmm-shaped contraction, and 3-operand
+    chains walked through those steps, give torch.einsum's result. (The
+    reference's matmul/bmm executors ignore the output order and the bmm
+    operands' index order.)"""
+    import itertools
+
+    torch.manual_seed(0)
+    sz = dict(i=3, j=4, k=5, l=6, b=2)
+    cases = []
+    for ta, tb, out in itertools.product(["ij", "ji"], ["jk", "kj"], ["ik", "ki"]):
+        cases.append(f"{ta},{tb}->{out}")
+    perms = [["".join(p) for p in itertools.permutations(t)] for t in ("bij", "bjk", "bik")]
+    for ta, tb, out in itertools.product(*perms):
+        cases.append(f"{ta},{tb}->{out}")
+    cases += ["ij,jk,kl->il", "ij,jk,kl->li", "bij,bjk,bkl->bil", "ij,jk->i"]
+    for s in cases:
+        ops = [torch.randn(*[sz[c] for c in t]) for t in s.split("->")[0].split(",")]
+        r, e = tt.einsum(s, *ops), torch.einsum(s, *ops)
+        assert r.shape == e.shape, s
+        assert torch.allclose(r, e, atol=1e-5), s

@@ -132,6 +132,38 @@ def _routes():
     assert tt.plan_contraction("ap,bp->ab", Bi, Bj).backend == "pytorch"
 
 
+def test_einsum_product_orders_on_tensor_cores(cuda_ok):
+    """Under set_backend("cuda") every index order of a matmul- or
+    bmm-shaped contraction reaches the tensor-core GEMM with the operands
+    brought into canonical form, and matches fp64 torch.einsum."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    A2 = torch.randn(70, 50, device="cuda", generator=g)   # (k, i)
+    B2 = torch.randn(60, 70, device="cuda", generator=g)   # (l, k)
+    X = torch.randn(50, 4, 60, device="cuda", generator=g)  # (i, b, j)
+    Y = torch.randn(70, 60, 4, device="cuda", generator=g)  # (k, j, b)
+    cases = [("ki,lk->il", A2, B2), ("ki,lk->li", A2, B2),
+             ("ibj,kjb->bki", X, Y), ("ibj,kjb->ikb", X, Y)]
+    tt.set_backend("cuda")
+    tt.clear_plan_cache()
+    try:
+        import trntensor_b200.dispatch as dp
+
+        for sub, a, b in cases:
+            calls = []
+            real = dp._cuda_gemm
+            dp._cuda_gemm = lambda *x: calls.append(x) or real(*x)  # noqa: E731
+            try:
+                got = tt.einsum(sub, a, b)
+            finally:
+                dp._cuda_gemm = real
+            ref = torch.einsum(sub, a.double(), b.double())
+            assert len(calls) == 1 and got.shape == ref.shape, sub
+            check(got, ref)
+    finally:
+        tt.set_backend("auto")
+        tt.clear_plan_cache()
+
+
 def test_path_steps_route_through_einsum(cuda_ok):
     """A 4-operand chain: the planner avoids outer products, and each binary
     step is planned again, so matmul-shaped steps reach the tensor-core GEMM

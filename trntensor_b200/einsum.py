@@ -107,23 +107,59 @@ def _execute(subscripts: str, operands: tuple, plan: ContractionPlan) -> torch.T
     if plan.precision == "dd":
         dt = operands[0].dtype if operands else torch.float32
         return _einsum_dd(subscripts, operands, plan).to(device=operands[0].device, dtype=dt)
-    if plan.strategy == "matmul":
-        A, B = operands
-        a, b = (A.T if plan.transA else A), (B.T if plan.transB else B)
+    if plan.strategy in ("matmul", "bmm"):
+        # Operands are brought into the canonical ([batch,] free, k) @
+        # ([batch,] k, free) form and the product into the requested output
+        # order. The plan's transA/transB flags (as the reference records
+        # them) only say where the contracted index sits; the reference's
+        # executors (trntensor/einsum.py:129-148) stop there, which returns
+        # (l, i) for 'kl,ik->il' and multiplies bmm operands as stored
+        # whatever their index order. Here every matmul- or bmm-shaped
+        # contraction gives torch.einsum's result.
+        pair = _canonical_pair(subscripts, operands, plan)
+        if pair is None:  # repeated or summed-out free indices: not a plain product
+            return torch.einsum(subscripts, *operands)
+        a, b, perm = pair
         if _tensor_core_ok(plan, a, b):
             from .dispatch import _cuda_gemm
 
-            return _cuda_gemm(a, b)
-        return torch.matmul(a, b)
-    if plan.strategy == "bmm":
-        if _tensor_core_ok(plan, *operands):
-            from .dispatch import _cuda_gemm
-
-            return _cuda_gemm(*operands)
-        return torch.bmm(*operands)
+            r = _cuda_gemm(a, b)
+        else:
+            r = torch.matmul(a, b)
+        return r if perm is None else r.permute(perm).contiguous()
     if plan.strategy == "path":
         return _execute_path(subscripts, operands, plan)
     return torch.einsum(subscripts, *operands)
+
+
+def _canonical_pair(subscripts: str, operands: tuple, plan: ContractionPlan):
+    """(a, b, perm): a = A as ([batch,] free_a, k), b = B as ([batch,] k,
+    free_b), and the permutation from the product's ([batch,] free_a,
+    free_b) order to the output's (None when it is already in order); None
+    when the contraction is not a plain (batched) product of distinct
+    indices."""
+    lhs, out = _parse_subscripts(subscripts)
+    ta, tb = lhs.split(",")
+    A, B = operands
+    k = plan.contraction_indices[0]
+    bt = plan.batch_indices[0] if plan.strategy == "bmm" else None
+    if len(set(ta)) != len(ta) or len(set(tb)) != len(tb) or len(set(out)) != len(out):
+        return None
+    fa = [c for c in ta if c not in (k, bt)]
+    fb = [c for c in tb if c not in (k, bt)]
+    if len(fa) != 1 or len(fb) != 1 or fa == fb:
+        return None
+    fa, fb = fa[0], fb[0]
+    if set(out) != {fa, fb} | ({bt} if bt is not None else set()):
+        return None
+    lead = [bt] if bt is not None else []
+    order_a = lead + [fa, k]
+    order_b = lead + [k, fb]
+    a = A.permute([ta.index(c) for c in order_a])
+    b = B.permute([tb.index(c) for c in order_b])
+    prod = lead + [fa, fb]
+    perm = [prod.index(c) for c in out]
+    return a, b, (None if perm == list(range(len(prod))) else perm)
 
 
 def _tensor_core_ok(plan: ContractionPlan, *ops: torch.Tensor) -> bool:
