@@ -77,6 +77,19 @@ def _worker(rank, world, port, mode, q):
                     local += float(sum(range(lo + 1, hi + 1)))
             distributed.reduce_energy(local)
             q.put((rank, local.item(), npairs * (npairs + 1) / 2))
+        elif mode == "blocks":
+            # the row-group block plan: each pair id contributes (id + 1) once
+            from trntensor_b200.dispatch import block_assignment, chunk_plan
+
+            nocc = 23
+            npairs = nocc * (nocc + 1) // 2
+            ranges, order = block_assignment(nocc, rank, world, chunks=6)
+            local = torch.zeros((), dtype=torch.float64)
+            for _, _, rr in chunk_plan(nocc, ranges, order):
+                for lo, hi in rr:
+                    local += float(sum(range(lo + 1, hi + 1)))
+            distributed.reduce_energy(local)
+            q.put((rank, local.item(), npairs * (npairs + 1) / 2))
         elif mode == "fail":
             if rank == 1:
                 raise RuntimeError("injected failure on rank 1 before the all-reduce")
@@ -141,7 +154,7 @@ def test_host_copy_plan_covers_each_ranks_pairs():
     by then, the rows copied must be exactly those host_bytes_needed counts,
     and pairs must be runnable after at most two chunks (so that the copy
     overlaps compute on every rank)."""
-    from trntensor_b200.dispatch import host_copy_plan
+    from trntensor_b200.dispatch import block_assignment, host_copy_plan
 
     for nocc in (1, 2, 5, 17, 64, 256):
         npairs = nocc * (nocc + 1) // 2
@@ -169,7 +182,62 @@ def test_host_copy_plan_covers_each_ranks_pairs():
                 assert sorted(covered) == list(range(pb, pe))  # each pair exactly once
                 rows = len(resident)
                 assert resident == set(range(nocc - rows, nocc))
-                assert rows * 7 * 3 * 4 == distributed.host_bytes_needed(nocc, 7, 3, rank, world)
+                if block_assignment(nocc, rank, world) is None:
+                    assert rows * 7 * 3 * 4 == distributed.host_bytes_needed(nocc, 7, 3, rank,
+                                                                             world)
                 # launches stay few: one range per step when the rank owns the last row
                 nranges = sum(len(r) for _, _, r in plan)
                 assert nranges <= len(plan) * max(1, nocc // world + 2)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_block_plan_energy_all_reduce(world):
+    """gloo ranks run the row-group block plan's ranges and all-reduce: every
+    pair id is counted exactly once over the job."""
+    for rank, got, want in _run(world, "blocks"):
+        assert got == want, rank
+
+
+def test_block_assignment_partition_balance_and_rows():
+    """At 4 and 8 ranks the row-group blocks partition all unordered pairs,
+    balance the work to within one group's diagonal, and need at most half
+    (8 ranks) or three quarters (4 ranks) of the rows; chunk_plan runs every
+    pair of a rank exactly once, after both of its rows have landed, and
+    something is runnable after the first two chunks."""
+    from trntensor_b200.dispatch import block_assignment, chunk_plan
+
+    for nocc in (8, 9, 23, 64, 256):
+        npairs = nocc * (nocc + 1) // 2
+        ids = [(i, j) for i in range(nocc) for j in range(i, nocc)]
+        for world in (4, 8):
+            seen = []
+            work = []
+            for rank in range(world):
+                ranges, order = block_assignment(nocc, rank, world)
+                mine = [p for lo, hi in ranges for p in range(lo, hi)]
+                seen += mine
+                work.append(len(mine))
+                rows = [r for a, b in order for r in range(a, b)]
+                assert len(rows) == len(set(rows))
+                limit = 0.5 if world == 8 or rank < 2 else 0.75
+                assert len(rows) <= limit * nocc + 2
+                assert set(rows) == {r for p in mine for r in ids[p]}
+                resident: set[int] = set()
+                covered = []
+                for step, (a, b, rr) in enumerate(chunk_plan(nocc, ranges, order)):
+                    resident |= set(range(a, b))
+                    for lo, hi in rr:
+                        for p in range(lo, hi):
+                            assert set(ids[p]) <= resident
+                        covered += range(lo, hi)
+                    if step == 1 and nocc >= 64:
+                        assert covered
+                assert sorted(covered) == sorted(mine)
+                assert distributed.host_bytes_needed(nocc, 7, 3, rank, world) == len(rows) * 84
+            assert sorted(seen) == list(range(npairs))
+            g = 4 if world == 8 else 2
+            assert max(work) - min(work) <= 2 * (-(-nocc // g))
+            if nocc == 256:
+                assert max(work) / min(work) <= 1.02
+    for world in (1, 2, 3):
+        assert block_assignment(256, 0, world) is None

@@ -247,3 +247,27 @@ def test_host_pipelined_copy(cuda_ok):
         a, _ = _cuda_mp2_energy(Bp, eo, ev, pair_range=rng)
         b, _ = _cuda_mp2_energy(B.cuda(), eo, ev, pair_range=rng)
         assert abs(a.item() - b.item()) <= 1e-12 * abs(ref.item())
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_host_block_plan_ranks_sum_to_energy(cuda_ok, world):
+    """Row-group blocks (the pair assignment of a host-resident B at 4 and 8
+    ranks): the ranks' energies, each run through the pipelined host copy in
+    its chunk order and, from a device copy, range by range, sum to the full
+    energy."""
+    from trntensor_b200.dispatch import block_assignment
+
+    nocc = 37
+    B, eo, ev = mp2_inputs(nocc, 300, 130, seed=6)
+    Bp = B.pin_memory()
+    ref, _ = _cuda_mp2_energy(B.cuda(), eo, ev)
+    tot_host = tot_dev = 0.0
+    for rank in range(world):
+        blocks = block_assignment(nocc, rank, world)
+        a, _ = _cuda_mp2_energy(Bp, eo, ev, blocks=blocks)
+        b, _ = _cuda_mp2_energy(B.cuda(), eo, ev, blocks=blocks)
+        assert abs(a.item() - b.item()) <= 1e-12 * abs(ref.item())
+        tot_host += a.item()
+        tot_dev += b.item()
+    assert rel(tot_host, ref.item()) <= 1e-12
+    assert rel(tot_dev, ref.item()) <= 1e-12

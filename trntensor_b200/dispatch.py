@@ -122,6 +122,7 @@ def _cuda_mp2_energy(
     pair_range: tuple[int, int] | None = None,
     return_partials: bool = False,
     kernel: str = "tc",
+    blocks=None,
 ):
     """Run the DF-MP2 energy on the current CUDA device.
 
@@ -131,8 +132,29 @@ def _cuda_mp2_energy(
     ``"tc"`` (int8 Ozaki tensor cores, the product path), ``"simt"`` (CUDA-core
     fp32 cross-check) or ``"tf32x3"`` (biased 3xTF32 diagnostic). For fp64
     (``precision="kahan"``) ``"tc"`` is the five-digit int8 Ozaki kernel and
-    ``"simt"`` the CUDA-core fp64 kernel.
+    ``"simt"`` the CUDA-core fp64 kernel. ``blocks`` (``block_assignment``'s
+    ``(ranges, chunk order)``) replaces ``pair_range`` by a set of ranges:
+    a host-resident B is then copied in that chunk order, a device-resident
+    one runs range by range.
     """
+    if blocks is not None and not (
+        B.device.type == "cpu" and B.is_pinned() and B.dtype == torch.float32
+        and B.is_contiguous() and mp2_compute_dtype(B, precision) == torch.float32
+        and kernel == "tc" and not return_partials
+    ):
+        if return_partials:
+            raise ValueError("blocks and return_partials cannot be combined")
+        dev = _device()
+        cdt = mp2_compute_dtype(B, precision)
+        Bd, eo, ev = _to_dev(B, dev, cdt), _to_dev(eps_occ, dev, cdt), _to_dev(eps_vir, dev, cdt)
+        tot = None
+        for rg in blocks[0]:
+            e, _ = _cuda_mp2_energy(Bd, eo, ev, precision=precision, pair_range=rg,
+                                    kernel=kernel)
+            tot = e if tot is None else tot + e
+        if tot is None:
+            tot = torch.zeros((), dtype=torch.float64, device=_device())
+        return tot, None
     lib = _lib.load()
     dev = _device()
     cdt = mp2_compute_dtype(B, precision)
@@ -146,7 +168,7 @@ def _cuda_mp2_energy(
     ):
         npairs = int(lib.tt_mp2_num_pairs(nocc))
         pb, pe = (0, npairs) if pair_range is None else (int(pair_range[0]), int(pair_range[1]))
-        return _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe), None
+        return _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, blocks=blocks), None
     Bd = _to_dev(B, dev, cdt)
     eo = _to_dev(eps_occ, dev, cdt)
     ev = _to_dev(eps_vir, dev, cdt)
@@ -254,6 +276,104 @@ def _merge(ranges: list[tuple[int, int]]) -> list[tuple[int, int]]:
     return out
 
 
+def _groups(nocc: int, g: int) -> list[tuple[int, int]]:
+    """g contiguous row groups [lo, hi) of nearly equal size."""
+    cuts = [round(k * nocc / g) for k in range(g + 1)]
+    return [(cuts[k], cuts[k + 1]) for k in range(g)]
+
+
+def _split(lo: int, hi: int, n: int) -> list[tuple[int, int]]:
+    """[lo, hi) in n contiguous chunks (fewer when there are fewer rows)."""
+    n = max(1, min(n, hi - lo))
+    cuts = [lo + round(k * (hi - lo) / n) for k in range(n + 1)]
+    return [(cuts[k], cuts[k + 1]) for k in range(n) if cuts[k + 1] > cuts[k]]
+
+
+def block_assignment(nocc: int, rank: int, world: int, chunks: int = 16):
+    """Pairs and row-copy order of ``rank`` when B is copied from the host.
+
+    With contiguous pair ranges the first rank's pairs touch every row of B,
+    so at 8 ranks rank 0 copies all of B (11.3 GB at BASELINE config 4,
+    ≈400 ms at the ≈25 GB/s a GPU gets while all eight copy) while the last
+    copies a sixth of it. For 4 and 8 ranks the rows are cut into row groups
+    instead, and each rank takes group pairs so that it needs half of the
+    rows (three quarters for two ranks at 4):
+
+    * 8 ranks, 4 groups: ranks 0-5 take the six off-diagonal group pairs
+      (Ga, Gb), a < b (all i in Ga, j in Gb); ranks 6 and 7 take the
+      diagonal blocks (G0, G0) + (G1, G1) and (G2, G2) + (G3, G3);
+    * 4 ranks, 2 groups: ranks 0 and 1 take (G0, G0) and (G1, G1), ranks 2
+      and 3 the two halves (by i) of (G0, G1).
+
+    Work per rank is equal to within one row group's diagonal (s² against
+    s² + s pairs for groups of s rows). Returns ``(ranges, chunks)``: the
+    rank's merged pair-id ranges and the row chunks [a, b) in copy order
+    (interleaved between the two groups of an off-diagonal pair, last rows
+    first within a diagonal block, so that pairs become runnable early), or
+    None when the contiguous ranges are used (other world sizes, or fewer
+    than two rows per group).
+    """
+    if world == 8:
+        g = 4
+        units = [((0, 1),), ((0, 2),), ((0, 3),), ((1, 2),), ((1, 3),), ((2, 3),),
+                 ((0, 0), (1, 1)), ((2, 2), (3, 3))]
+    elif world == 4:
+        g = 2
+        units = [((0, 0),), ((1, 1),), ((0, 1, 0),), ((0, 1, 1),)]
+    else:
+        return None
+    if nocc < 2 * g:
+        return None
+    grp = _groups(nocc, g)
+    pairs: list[tuple[int, int]] = []
+    order: list[tuple[int, int]] = []
+    for u in units[rank]:
+        a, b = u[0], u[1]
+        ga, gb = grp[a], grp[b]
+        if len(u) == 3:  # half (by i) of an off-diagonal group pair
+            ga = _split(ga[0], ga[1], 2)[u[2]]
+        if a == b:
+            for i in range(ga[0], ga[1]):
+                pairs.append((pair_offset(i, nocc), pair_offset(i, nocc) + ga[1] - i))
+            order += _split(ga[0], ga[1], max(1, chunks // len(units[rank])))[::-1]
+        else:
+            for i in range(ga[0], ga[1]):
+                pairs.append((pair_offset(i, nocc) + gb[0] - i, pair_offset(i, nocc) + gb[1] - i))
+            ca = _split(ga[0], ga[1], max(1, chunks // 2))
+            cb = _split(gb[0], gb[1], max(1, chunks // 2))
+            for k in range(max(len(ca), len(cb))):
+                order += ca[k:k + 1] + cb[k:k + 1]
+    return _merge(sorted(pairs)), order
+
+
+def chunk_plan(nocc: int, ranges: list[tuple[int, int]], order: list[tuple[int, int]]):
+    """Copy plan in host_copy_plan's format for the pair-id ``ranges`` when
+    rows are copied in the chunk ``order``: after each chunk, the ranges of
+    the pairs whose later row has just landed."""
+    step_of = [-1] * nocc
+    for k, (a, b) in enumerate(order):
+        for r in range(a, b):
+            step_of[r] = k
+    runs: list[list[tuple[int, int]]] = [[] for _ in order]
+    for lo, hi in ranges:
+        i = first_row_of_pair(lo, nocc)
+        p = lo
+        while p < hi:
+            end = min(hi, pair_offset(i + 1, nocc))
+            si = step_of[i]
+            j = i + (p - pair_offset(i, nocc))
+            while p < end:  # runs of consecutive j landing in the same step
+                k = max(si, step_of[j])
+                q = p
+                while q < end and max(si, step_of[j + (q - p)]) == k:
+                    q += 1
+                runs[k].append((p, q))
+                j += q - p
+                p = q
+            i += 1
+    return [(a, b, _merge(sorted(r))) for (a, b), r in zip(order, runs)]
+
+
 def host_copy_plan(nocc: int, pb: int, pe: int, chunks: int = 16):
     """Copy order of a host B's rows for the pairs [pb, pe), and what to run.
 
@@ -344,10 +464,12 @@ def _needs_more_digits(stats: torch.Tensor, naux: int) -> bool:
     return _wide_rows_estimate(stats.tolist(), naux) > WIDE_ROWS_MAX_EST
 
 
-def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
+def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16, blocks=None):
     """fp32 DF-MP2 energy of host-resident pinned B with the copy overlapped.
 
-    Rows are copied on a side stream in the order of ``host_copy_plan``;
+    Rows are copied on a side stream in the order of ``host_copy_plan`` (the
+    pair range [pb, pe)) or, with ``blocks = (ranges, chunk order)`` from
+    ``block_assignment``, of ``chunk_plan``;
     each chunk is split into int8 slices as it lands (tt_split_i8_rows) and
     the pairs it completes run on the current stream while the next chunk is
     in flight. Only the rows the pair range needs are copied. If the range
@@ -359,7 +481,8 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
     sp = ctypes.c_void_p(stream.cuda_stream)
     eo = _to_dev(eps_occ, dev, torch.float32)
     ev = _to_dev(eps_vir, dev, torch.float32)
-    if pe <= pb:
+    all_ranges = [(pb, pe)] if blocks is None else [r for r in blocks[0] if r[1] > r[0]]
+    if not all_ranges or all_ranges[0][1] <= all_ranges[0][0]:
         return torch.zeros((), dtype=torch.float64, device=dev)
     pad = (naux + 63) // 64 * 64
     rows_total = nocc * nvir
@@ -368,11 +491,22 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
     qbytes = (3 * rows_total * pad + 255) // 256 * 256
     q_ptr = ws.data_ptr()
     s_ptr = ws.data_ptr() + qbytes
-    plan = host_copy_plan(nocc, pb, pe, chunks)
-    i0 = min(a for a, _, _ in plan)
+    plan = (host_copy_plan(nocc, pb, pe, chunks) if blocks is None
+            else chunk_plan(nocc, blocks[0], blocks[1]))
     Bd = torch.empty((nocc, nvir, naux), dtype=torch.float32, device=dev)
-    if i0 > 0:
-        Bd[:i0].zero_()  # rows no pair of the range reads (keeps a recompute clean)
+    copied = [False] * nocc
+    for a, b, _ in plan:
+        copied[a:b] = [True] * (b - a)
+    r = 0
+    while r < nocc:  # rows no pair of the rank reads (keeps a recompute clean)
+        if copied[r]:
+            r += 1
+            continue
+        e = r
+        while e < nocc and not copied[e]:
+            e += 1
+        Bd[r:e].zero_()
+        r = e
     nlaunch = sum(len(r) for _, _, r in plan)
     energies = torch.zeros(max(1, nlaunch), dtype=torch.float64, device=dev)
     status = torch.zeros(max(1, nlaunch), dtype=torch.int32, device=dev)
@@ -406,7 +540,8 @@ def _mp2_host_pipelined(lib, dev, B, eps_occ, eps_vir, pb, pe, chunks=16):
                                    f"(status 0x{int(status[bad[0, 0]].item()):x})")
     if _needs_more_digits(stats, naux):
         del ws
-        energy, _ = _cuda_mp2_energy(Bd, eo, ev, precision="kahan", pair_range=(pb, pe))
+        energy = sum(_cuda_mp2_energy(Bd, eo, ev, precision="kahan", pair_range=rg)[0]
+                     for rg in all_ranges)
     return energy
 
 

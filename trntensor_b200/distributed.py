@@ -2,8 +2,10 @@
 
 * ``mp2_energy``: B is replicated on every rank; the unordered occupied
   pairs (i <= j, row-major linear ids) are split into equal contiguous
-  ranges, each rank runs the fused kernel on its range, and one fp64 scalar
-  is summed across ranks (NCCL all-reduce on GPUs, gloo on CPU).
+  ranges (or, for a host-resident B at 4 and 8 ranks, into row-group
+  blocks that halve what each rank copies), each rank runs the fused
+  kernel on its pairs, and one fp64 scalar is summed across ranks (NCCL
+  all-reduce on GPUs, gloo on CPU).
 * ``ao_to_mo_transform``: each rank transforms its own slab of the
   auxiliary index P; there is no communication. ``aux_slab`` gives the slab.
 
@@ -15,7 +17,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from .dispatch import _cuda_mp2_energy
+from .dispatch import _cuda_mp2_energy, block_assignment
 
 
 def _world(group=None) -> tuple[int, int]:
@@ -37,9 +39,14 @@ def aux_slab(naux: int, rank: int, world: int) -> tuple[int, int]:
 
 
 def host_bytes_needed(nocc: int, nvir: int, naux: int, rank: int, world: int) -> int:
-    """Bytes of a host fp32 B a rank copies: rows first_row(pair_begin)..nocc-1."""
+    """Bytes of a host fp32 B a rank copies in ``mp2_energy``: the rows of its
+    row-group blocks (``block_assignment``, 4 and 8 ranks), else rows
+    first_row(pair_begin)..nocc-1 of its contiguous pair range."""
     from .dispatch import first_row_of_pair
 
+    blocks = block_assignment(nocc, rank, world)
+    if blocks is not None:
+        return sum(b - a for a, b in blocks[1]) * nvir * naux * 4
     pb, pe = pair_range(nocc * (nocc + 1) // 2, rank, world)
     if pe <= pb:
         return 0
@@ -75,8 +82,13 @@ def mp2_energy(
     if B.numel() == 0:  # same shapes on every rank: all of them return here
         return B.new_zeros(())
     npairs = nocc * (nocc + 1) // 2
+    # A host-resident B is copied by every rank: at 4 and 8 ranks the pairs
+    # are assigned by row-group blocks so that each rank copies about half
+    # of B (block_assignment); on the device the contiguous ranges are kept.
+    blocks = block_assignment(nocc, rank, world) if B.device.type == "cpu" else None
     e, _ = _cuda_mp2_energy(
-        B, eps_occ, eps_vir, precision=precision, pair_range=pair_range(npairs, rank, world)
+        B, eps_occ, eps_vir, precision=precision, pair_range=pair_range(npairs, rank, world),
+        blocks=blocks,
     )
     reduce_energy(e, group)
     return e.to(device=B.device, dtype=B.dtype)
